@@ -1,0 +1,145 @@
+// cwg_common.cuh -- shared device helpers: Winograd tables, element I/O,
+// launch bookkeeping.  Device code for sm_100a only.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cwg_internal.h"
+
+namespace cwg {
+
+// ---- element conversion -----------------------------------------------------
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// ---- Winograd tables ----------------------------------------------------------
+// Bt (td x td) and At (m x td) are the reference's tables
+// (src/fused_winograd_kernel.py:18-67).  They are spelled out as local
+// constant arrays so that, once the loops are unrolled, every coefficient is a
+// compile-time immediate and the zero terms vanish.
+template <int M>
+struct Wino;
+
+template <>
+struct Wino<2> {
+  static constexpr int TD = 4;
+  __device__ __forceinline__ static float bt(int a, int i) {
+    const float t[4][4] = {{1, 0, -1, 0}, {0, 1, 1, 0}, {0, -1, 1, 0}, {0, 1, 0, -1}};
+    return t[a][i];
+  }
+  __device__ __forceinline__ static float at(int a, int i) {
+    const float t[2][4] = {{1, 1, 1, 0}, {0, 1, -1, -1}};
+    return t[a][i];
+  }
+};
+
+template <>
+struct Wino<4> {
+  static constexpr int TD = 6;
+  __device__ __forceinline__ static float bt(int a, int i) {
+    const float t[6][6] = {{4, 0, -5, 0, 1, 0},  {0, -4, -4, 1, 1, 0}, {0, 4, -4, -1, 1, 0},
+                           {0, -2, -1, 2, 1, 0}, {0, 2, -1, -2, 1, 0}, {0, 4, 0, -5, 0, 1}};
+    return t[a][i];
+  }
+  __device__ __forceinline__ static float at(int a, int i) {
+    const float t[4][6] = {
+        {1, 1, 1, 1, 1, 0}, {0, 1, -1, 2, -2, 0}, {0, 1, 1, 4, 4, 0}, {0, 1, -1, 8, -8, 1}};
+    return t[a][i];
+  }
+};
+
+template <>
+struct Wino<6> {
+  static constexpr int TD = 8;
+  __device__ __forceinline__ static float bt(int a, int i) {
+    const float t[8][8] = {{1, 0, -5.25f, 0, 5.25f, 0, -1, 0},
+                           {0, 1, 1, -4.25f, -4.25f, 1, 1, 0},
+                           {0, -1, 1, 4.25f, -4.25f, -1, 1, 0},
+                           {0, 0.5f, 0.25f, -2.5f, -1.25f, 2, 1, 0},
+                           {0, -0.5f, 0.25f, 2.5f, -1.25f, -2, 1, 0},
+                           {0, 2, 4, -2.5f, -5, 0.5f, 1, 0},
+                           {0, -2, 4, 2.5f, -5, -0.5f, 1, 0},
+                           {0, -1, 0, 5.25f, 0, -5.25f, 0, 1}};
+    return t[a][i];
+  }
+  __device__ __forceinline__ static float at(int a, int i) {
+    const float t[6][8] = {{1, 1, 1, 1, 1, 32, 32, 0},   {0, 1, -1, 2, -2, 16, -16, 0},
+                           {0, 1, 1, 4, 4, 8, 8, 0},     {0, 1, -1, 8, -8, 4, -4, 0},
+                           {0, 1, 1, 16, 16, 2, 2, 0},   {0, 1, -1, 32, -32, 1, -1, 1}};
+    return t[a][i];
+  }
+};
+
+// s + c*d.  EXACT keeps the reference's separate multiply and add (two
+// roundings, as the reference's C compiles on x86-64); otherwise one FMA.
+template <bool EXACT>
+__device__ __forceinline__ float madd(float c, float d, float s) {
+  return EXACT ? __fadd_rn(s, __fmul_rn(c, d)) : fmaf(c, d, s);
+}
+
+// v = Bt d B (td x td, row-major), sequential in the reference's index order.
+template <int M, bool EXACT = false>
+__device__ __forceinline__ void input_transform(const float (&d)[M + 2][M + 2],
+                                                float (&v)[M + 2][M + 2]) {
+  constexpr int TD = M + 2;
+  float t[TD][TD];
+#pragma unroll
+  for (int a = 0; a < TD; ++a)
+#pragma unroll
+    for (int j = 0; j < TD; ++j) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < TD; ++i)
+        if (Wino<M>::bt(a, i) != 0.f) s = madd<EXACT>(Wino<M>::bt(a, i), d[i][j], s);
+      t[a][j] = s;
+    }
+#pragma unroll
+  for (int a = 0; a < TD; ++a)
+#pragma unroll
+    for (int b = 0; b < TD; ++b) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < TD; ++j)
+        if (Wino<M>::bt(b, j) != 0.f) s = madd<EXACT>(Wino<M>::bt(b, j), t[a][j], s);
+      v[a][b] = s;
+    }
+}
+
+// y = At m A (m x m) from the td x td accumulator tile.
+template <int M, bool EXACT = false>
+__device__ __forceinline__ void output_transform(const float (&mm)[M + 2][M + 2],
+                                                 float (&y)[M][M]) {
+  constexpr int TD = M + 2;
+  float t[M][TD];
+#pragma unroll
+  for (int i = 0; i < M; ++i)
+#pragma unroll
+    for (int b = 0; b < TD; ++b) {
+      float s = 0.f;
+#pragma unroll
+      for (int a = 0; a < TD; ++a)
+        if (Wino<M>::at(i, a) != 0.f) s = madd<EXACT>(Wino<M>::at(i, a), mm[a][b], s);
+      t[i][b] = s;
+    }
+#pragma unroll
+  for (int i = 0; i < M; ++i)
+#pragma unroll
+    for (int j = 0; j < M; ++j) {
+      float s = 0.f;
+#pragma unroll
+      for (int b = 0; b < TD; ++b)
+        if (Wino<M>::at(j, b) != 0.f) s = madd<EXACT>(Wino<M>::at(j, b), t[i][b], s);
+      y[i][j] = s;
+    }
+}
+
+}  // namespace cwg

@@ -1,0 +1,455 @@
+// cwg_ffma.cu -- CUDA-core kernels of libcwg:
+//   * wt_transform        U = G g G^T (or an import of a reference-layout U)
+//   * wino_fused_ffma     the fused layer kernel for small channel counts
+//                         (halo load -> Bt d B -> per-frequency register-blocked
+//                         FFMA GEMMs -> At M A + bias + ReLU -> store)
+//   * tiles_fused         the reference's per-tile operation on device buffers
+// plus the launch shims declared in cwg_internal.h.
+#include <atomic>
+#include <cstdio>
+
+#include "cwg_common.cuh"
+
+namespace cwg {
+
+// Device-side status word.  Bounded waits in the tensor-core kernel set bit 0
+// when they give up; cwg_device_status() reads and clears it.
+__device__ unsigned int g_status;
+
+static std::atomic<long long> g_launches{0};
+static thread_local int t_cuda_error = 0;
+
+// ============================================================================
+// Weight transform
+// ============================================================================
+// G for F(2,3) and F(4,3): the unique matrices that make the reference's Bt/At
+// (src/fused_winograd_kernel.py:18-46) compute a 3x3 cross-correlation.
+template <int M>
+__device__ __forceinline__ double gmat(int a, int i);
+template <>
+__device__ __forceinline__ double gmat<2>(int a, int i) {
+  const double g[4][3] = {{1, 0, 0}, {.5, .5, .5}, {.5, -.5, .5}, {0, 0, 1}};
+  return g[a][i];
+}
+template <>
+__device__ __forceinline__ double gmat<4>(int a, int i) {
+  const double g[6][3] = {{1. / 4, 0, 0},          {-1. / 6, -1. / 6, -1. / 6},
+                          {-1. / 6, 1. / 6, -1. / 6}, {1. / 24, 1. / 12, 1. / 6},
+                          {1. / 24, -1. / 12, 1. / 6}, {0, 0, 1}};
+  return g[a][i];
+}
+
+// u[f] for one (k, c) pair, in fp64 with the same operation order as the CPU
+// oracle (no contraction), rounded once to fp32.
+template <int M>
+__device__ __forceinline__ void transform_one(const float *src, int from_ref, float *u) {
+  constexpr int TD = M + 2, NF = TD * TD;
+  if (from_ref) {
+#pragma unroll
+    for (int f = 0; f < NF; ++f) u[f] = src[f];
+    return;
+  }
+  double gk[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) gk[i] = (double)src[i];
+  double t[TD][3];
+#pragma unroll
+  for (int a = 0; a < TD; ++a)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      double s = 0.0;
+#pragma unroll
+      for (int i = 0; i < 3; ++i) s = __dadd_rn(s, __dmul_rn(gmat<M>(a, i), gk[i * 3 + j]));
+      t[a][j] = s;
+    }
+#pragma unroll
+  for (int a = 0; a < TD; ++a)
+#pragma unroll
+    for (int b = 0; b < TD; ++b) {
+      double s = 0.0;
+#pragma unroll
+      for (int j = 0; j < 3; ++j) s = __dadd_rn(s, __dmul_rn(t[a][j], gmat<M>(b, j)));
+      u[a * TD + b] = (float)s;
+    }
+}
+
+// One thread per (c, k); k fastest so the [f][C][K] stores coalesce.
+template <int M, typename Tu>
+__global__ void wt_transform_ffma(const float *__restrict__ src, Tu *__restrict__ U, int C,
+                                  int K, int from_ref) {
+  constexpr int NF = (M + 2) * (M + 2);
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)C * K) return;
+  const int k = (int)(idx % K), c = (int)(idx / K);
+  float u[NF];
+  transform_one<M>(src + ((long)k * C + c) * (from_ref ? NF : 9), from_ref, u);
+#pragma unroll
+  for (int f = 0; f < NF; ++f) U[((long)f * C + c) * K + k] = from_f32<Tu>(u[f]);
+}
+
+// ============================================================================
+// Fused FFMA kernel
+// ============================================================================
+// CTA = TY x TX output tiles of one image x KB output channels.  Per step of CC
+// input channels: the (TY*M+2) x (TX*M+2) halo is staged in shared memory
+// (zero outside the image = pad 1), each (channel, tile) is transformed to V,
+// and every warp runs the GEMM of FPW frequencies, each lane holding a TR x KR
+// register block (tiles x channels).  The epilogue regroups the frequency
+// accumulators through shared memory, applies At M A, bias and ReLU, and
+// stores NCHW.
+template <int M, int TY, int TX, int KB, int CC, int FPW>
+struct FG {
+  static constexpr int TD = M + 2, NF = TD * TD, T = TY * TX;
+  static constexpr int HR = TY * M + 2, WR = TX * M + 2;
+  static constexpr int KR = 4, KG = KB / KR, TG = 32 / KG, TR = T / TG;
+  static constexpr int NW = NF / FPW, NT = NW * 32;
+  static constexpr int XS = CC * HR * WR, VS = NF * CC * T, US = NF * CC * KB;
+  static constexpr int MAIN = XS + VS + US;
+  static constexpr int EPI = NF * KG * (T + 1);
+  static constexpr int SMEM = 4 * (MAIN > EPI ? MAIN : EPI);
+  static_assert(NF % FPW == 0, "frequencies per warp must divide td^2");
+  static_assert(KB % KR == 0 && 32 % KG == 0 && T % TG == 0, "lane grid must tile 32");
+  static_assert(TR == 2 || TR % 4 == 0, "tile register block must vectorise");
+};
+
+template <int N>
+__device__ __forceinline__ void lds_vec(const float *p, float (&v)[N]) {
+  if constexpr (N == 2) {
+    const float2 a = *reinterpret_cast<const float2 *>(p);
+    v[0] = a.x;
+    v[1] = a.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      const float4 a = *reinterpret_cast<const float4 *>(p + i);
+      v[i] = a.x;
+      v[i + 1] = a.y;
+      v[i + 2] = a.z;
+      v[i + 3] = a.w;
+    }
+  }
+}
+
+template <int M, int TY, int TX, int KB, int CC, int FPW, typename Tio>
+__global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
+    wino_fused_ffma(const Tio *__restrict__ x, const Tio *__restrict__ U,
+                    const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
+                    int W, int tiles_y, int tiles_x, int relu) {
+  using G = FG<M, TY, TX, KB, CC, FPW>;
+  constexpr int TD = G::TD, T = G::T, NT = G::NT, KR = G::KR, TR = G::TR, KG = G::KG;
+  extern __shared__ __align__(16) float smem[];
+  float *xs = smem;
+  float *vs = xs + G::XS;
+  float *us = vs + G::VS;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tg = lane / KG, kg = lane % KG;
+  const int nbx = (tiles_x + TX - 1) / TX;
+  const int by = blockIdx.x / nbx, bx = blockIdx.x - by * nbx;
+  const int k0 = blockIdx.y * KB, n = blockIdx.z;
+  const int ty0 = by * TY, tx0 = bx * TX;
+  const int iy0 = ty0 * M - 1, ix0 = tx0 * M - 1;
+  const size_t plane = (size_t)H * W;
+  const Tio *xn = x + (size_t)n * C * plane;
+
+  float acc[FPW][TR][KR];
+#pragma unroll
+  for (int a = 0; a < FPW; ++a)
+#pragma unroll
+    for (int b = 0; b < TR; ++b)
+#pragma unroll
+      for (int c = 0; c < KR; ++c) acc[a][b][c] = 0.f;
+
+  for (int c0 = 0; c0 < C; c0 += CC) {
+    // stage the input halo (zero outside the image and past C)
+    for (int i = tid; i < G::XS; i += NT) {
+      const int c = i / (G::HR * G::WR), rem = i - c * (G::HR * G::WR);
+      const int r = rem / G::WR, s = rem - r * G::WR;
+      const int iy = iy0 + r, ix = ix0 + s;
+      float v = 0.f;
+      if (c0 + c < C && iy >= 0 && iy < H && ix >= 0 && ix < W)
+        v = to_f32(xn[(size_t)(c0 + c) * plane + (size_t)iy * W + ix]);
+      xs[i] = v;
+    }
+    // stage U[f][c0:c0+CC][k0:k0+KB]
+    for (int i = tid; i < G::US; i += NT) {
+      const int k = i % KB, fc = i / KB, c = fc % CC, f = fc / CC;
+      float v = 0.f;
+      if (c0 + c < C && k0 + k < K) v = to_f32(U[((size_t)f * C + c0 + c) * K + k0 + k]);
+      us[i] = v;
+    }
+    __syncthreads();
+    // input transform: one (channel, tile) per thread
+    for (int p = tid; p < CC * T; p += NT) {
+      const int c = p / T, t = p - c * T, tyl = t / TX, txl = t - tyl * TX;
+      const float *src = xs + c * G::HR * G::WR + (tyl * M) * G::WR + txl * M;
+      float d[TD][TD], v[TD][TD];
+#pragma unroll
+      for (int r = 0; r < TD; ++r)
+#pragma unroll
+        for (int s = 0; s < TD; ++s) d[r][s] = src[r * G::WR + s];
+      input_transform<M>(d, v);
+#pragma unroll
+      for (int a = 0; a < TD; ++a)
+#pragma unroll
+        for (int b = 0; b < TD; ++b) vs[((a * TD + b) * CC + c) * T + t] = v[a][b];
+    }
+    __syncthreads();
+    // per-frequency GEMM on the CUDA cores
+#pragma unroll 2
+    for (int c = 0; c < CC; ++c) {
+#pragma unroll
+      for (int fi = 0; fi < FPW; ++fi) {
+        const int f = warp * FPW + fi;
+        float vv[TR], uu[KR];
+        lds_vec<TR>(vs + (f * CC + c) * T + tg * TR, vv);
+        lds_vec<KR>(us + (f * CC + c) * KB + kg * KR, uu);
+#pragma unroll
+        for (int r = 0; r < TR; ++r)
+#pragma unroll
+          for (int q = 0; q < KR; ++q) acc[fi][r][q] = fmaf(vv[r], uu[q], acc[fi][r][q]);
+      }
+    }
+    __syncthreads();
+  }
+
+  // epilogue: regroup the NF accumulators of each (tile, channel), one
+  // register column q at a time, then At M A + bias + ReLU.
+  float *ms = smem;  // [NF][KG][T+1]
+#pragma unroll
+  for (int q = 0; q < KR; ++q) {
+#pragma unroll
+    for (int fi = 0; fi < FPW; ++fi)
+#pragma unroll
+      for (int r = 0; r < TR; ++r)
+        ms[((warp * FPW + fi) * KG + kg) * (T + 1) + tg * TR + r] = acc[fi][r][q];
+    __syncthreads();
+    for (int p = tid; p < T * KG; p += NT) {
+      const int t = p % T, kgp = p / T;
+      const int k = k0 + kgp * KR + q;
+      const int tyl = t / TX, txl = t - tyl * TX;
+      const int ty = ty0 + tyl, tx = tx0 + txl;
+      if (k < K && ty < tiles_y && tx < tiles_x) {
+        float mm[TD][TD], yy[M][M];
+#pragma unroll
+        for (int a = 0; a < TD; ++a)
+#pragma unroll
+          for (int b = 0; b < TD; ++b) mm[a][b] = ms[((a * TD + b) * KG + kgp) * (T + 1) + t];
+        output_transform<M>(mm, yy);
+        const float bb = bias ? bias[k] : 0.f;
+        Tio *yk = y + ((size_t)n * K + k) * plane;
+#pragma unroll
+        for (int i = 0; i < M; ++i)
+#pragma unroll
+          for (int j = 0; j < M; ++j) {
+            const int oy = ty * M + i, ox = tx * M + j;
+            if (oy < H && ox < W) {
+              float v = yy[i][j] + bb;
+              if (relu) v = v < 0.f ? 0.f : v;
+              yk[(size_t)oy * W + ox] = from_f32<Tio>(v);
+            }
+          }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ============================================================================
+// Per-tile kernel (reference layouts; fused_winograd.c:19-101 semantics)
+// ============================================================================
+// CTA = one tile x 128 output channels; thread = one output channel.  V for a
+// chunk of input channels is staged in shared memory; the accumulation over
+// input channels is sequential with the reference's zero-skip and separate
+// multiply/add, so F(2,3) reproduces the reference C bit for bit.
+constexpr int kTileThreads = 128;
+constexpr int kTileChunk = 64;
+
+template <int M>
+__global__ void __launch_bounds__(kTileThreads)
+    tiles_fused(const float *__restrict__ tiles, const float *__restrict__ U,
+                float *__restrict__ out, int C, int K) {
+  constexpr int TD = M + 2, NF = TD * TD;
+  __shared__ float vsh[kTileChunk * NF];
+  const int tile = blockIdx.x;
+  const int oc = blockIdx.y * kTileThreads + threadIdx.x;
+  const float *in = tiles + (size_t)tile * C * NF;
+  float acc[NF];
+#pragma unroll
+  for (int f = 0; f < NF; ++f) acc[f] = 0.f;
+  for (int c0 = 0; c0 < C; c0 += kTileChunk) {
+    const int cn = min(kTileChunk, C - c0);
+    __syncthreads();
+    for (int ic = threadIdx.x; ic < cn; ic += kTileThreads) {
+      float d[TD][TD], v[TD][TD];
+#pragma unroll
+      for (int r = 0; r < TD; ++r)
+#pragma unroll
+        for (int s = 0; s < TD; ++s) d[r][s] = in[(size_t)(c0 + ic) * NF + r * TD + s];
+      input_transform<M, true>(d, v);
+#pragma unroll
+      for (int a = 0; a < TD; ++a)
+#pragma unroll
+        for (int b = 0; b < TD; ++b) vsh[ic * NF + a * TD + b] = v[a][b];
+    }
+    __syncthreads();
+    if (oc < K) {
+      const float *u = U + ((size_t)oc * C + c0) * NF;
+      for (int ic = 0; ic < cn; ++ic) {
+#pragma unroll
+        for (int f = 0; f < NF; ++f) {
+          const float uf = u[(size_t)ic * NF + f];
+          if (uf != 0.0f) acc[f] = __fadd_rn(acc[f], __fmul_rn(uf, vsh[ic * NF + f]));
+        }
+      }
+    }
+  }
+  if (oc < K) {
+    float mm[TD][TD], yy[M][M];
+#pragma unroll
+    for (int a = 0; a < TD; ++a)
+#pragma unroll
+      for (int b = 0; b < TD; ++b) mm[a][b] = acc[a * TD + b];
+    output_transform<M, true>(mm, yy);
+    float *o = out + ((size_t)tile * K + oc) * M * M;
+#pragma unroll
+    for (int i = 0; i < M; ++i)
+#pragma unroll
+      for (int j = 0; j < M; ++j) o[i * M + j] = yy[i][j];
+  }
+}
+
+// ============================================================================
+// Configuration table + launch shims
+// ============================================================================
+typedef void (*ffma_fn)(const void *, const void *, const float *, void *, int, int, int, int,
+                        int, int, int);
+
+struct FfmaEntry {
+  cwgk_ffma_cfg cfg;
+  const void *fn_f32;
+  const void *fn_bf16;
+};
+
+#define CWG_FFMA_ENTRY(M_, TY_, TX_, KB_, CC_, FPW_)                                         \
+  {{M_, TY_, TX_, KB_, CC_, FG<M_, TY_, TX_, KB_, CC_, FPW_>::NT,                            \
+    FG<M_, TY_, TX_, KB_, CC_, FPW_>::SMEM},                                                 \
+   (const void *)wino_fused_ffma<M_, TY_, TX_, KB_, CC_, FPW_, float>,                      \
+   (const void *)wino_fused_ffma<M_, TY_, TX_, KB_, CC_, FPW_, __nv_bfloat16>}
+
+static const FfmaEntry kFfma[] = {
+    CWG_FFMA_ENTRY(2, 4, 4, 16, 8, 1), CWG_FFMA_ENTRY(2, 4, 4, 32, 8, 1),
+    CWG_FFMA_ENTRY(2, 4, 4, 64, 8, 1), CWG_FFMA_ENTRY(2, 8, 8, 32, 8, 1),
+    CWG_FFMA_ENTRY(4, 4, 4, 16, 8, 2), CWG_FFMA_ENTRY(4, 4, 4, 32, 8, 2),
+    CWG_FFMA_ENTRY(4, 4, 4, 64, 8, 2),
+};
+constexpr int kNumFfma = sizeof(kFfma) / sizeof(kFfma[0]);
+
+static int fail(cudaError_t e) {
+  t_cuda_error = (int)e;
+  return -3; /* CWG_ECUDA */
+}
+
+}  // namespace cwg
+
+using namespace cwg;
+
+extern "C" {
+
+void cwgk_count_launch(void) { g_launches.fetch_add(1, std::memory_order_relaxed); }
+long long cwgk_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+void cwgk_set_cuda_error(int err) { t_cuda_error = err; }
+int cwgk_get_cuda_error(void) { return t_cuda_error; }
+
+int cwgk_ffma_num_cfgs(void) { return kNumFfma; }
+
+int cwgk_ffma_get_cfg(int idx, cwgk_ffma_cfg *out) {
+  if (idx < 0 || idx >= kNumFfma || !out) return -1;
+  *out = kFfma[idx].cfg;
+  return 0;
+}
+
+int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m, int layout,
+                          int from_ref, void *stream) {
+  if (layout != CWGK_LAYOUT_FFMA_F32 && layout != CWGK_LAYOUT_FFMA_BF16) return -2;
+  const long total = (long)c_in * c_out;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)((total + threads - 1) / threads);
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool bf = layout == CWGK_LAYOUT_FFMA_BF16;
+  if (m == 2) {
+    if (bf)
+      wt_transform_ffma<2, __nv_bfloat16>
+          <<<blocks, threads, 0, s>>>(src, (__nv_bfloat16 *)U, c_in, c_out, from_ref);
+    else
+      wt_transform_ffma<2, float><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out,
+                                                             from_ref);
+  } else if (m == 4) {
+    if (bf)
+      wt_transform_ffma<4, __nv_bfloat16>
+          <<<blocks, threads, 0, s>>>(src, (__nv_bfloat16 *)U, c_in, c_out, from_ref);
+    else
+      wt_transform_ffma<4, float><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out,
+                                                             from_ref);
+  } else {
+    return -2;
+  }
+  cwgk_count_launch();
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : fail(e);
+}
+
+int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
+                   int c_in, int c_out, int h, int w, int bf16, int relu, void *stream) {
+  if (cfg_idx < 0 || cfg_idx >= kNumFfma) return -1;
+  const FfmaEntry &e = kFfma[cfg_idx];
+  const int m = e.cfg.m;
+  const int tiles_y = (h + m - 1) / m, tiles_x = (w + m - 1) / m;
+  const unsigned gx = (unsigned)(((tiles_y + e.cfg.ty - 1) / e.cfg.ty) *
+                                 ((tiles_x + e.cfg.tx - 1) / e.cfg.tx));
+  const unsigned gy = (unsigned)((c_out + e.cfg.kb - 1) / e.cfg.kb);
+  if (n > 65535 || gy > 65535) return -2;
+  const void *fn = bf16 ? e.fn_bf16 : e.fn_f32;
+  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         e.cfg.smem);
+  if (err != cudaSuccess) return fail(err);
+  void *args[] = {(void *)&x,  (void *)&U, (void *)&bias,    (void *)&y,       (void *)&c_in,
+                  (void *)&c_out, (void *)&h, (void *)&w, (void *)&tiles_y, (void *)&tiles_x,
+                  (void *)&relu};
+  err = cudaLaunchKernel(fn, dim3(gx, gy, (unsigned)n), dim3((unsigned)e.cfg.threads), args,
+                         (size_t)e.cfg.smem, (cudaStream_t)stream);
+  cwgk_count_launch();
+  return err == cudaSuccess ? 0 : fail(err);
+}
+
+int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,
+               int td, void *stream) {
+  if (n_tiles == 0) return 0;
+  if (n_tiles > 0x7fffffff || c_out <= 0) return -1;
+  const dim3 grid((unsigned)n_tiles, (unsigned)((c_out + kTileThreads - 1) / kTileThreads));
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (td) {
+    case 4: tiles_fused<2><<<grid, kTileThreads, 0, s>>>(tiles, U, out, c_in, c_out); break;
+    case 6: tiles_fused<4><<<grid, kTileThreads, 0, s>>>(tiles, U, out, c_in, c_out); break;
+    case 8: tiles_fused<6><<<grid, kTileThreads, 0, s>>>(tiles, U, out, c_in, c_out); break;
+    default: return -2;
+  }
+  cwgk_count_launch();
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : fail(e);
+}
+
+int cwgk_read_clear_status(unsigned *status) {
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+  if (e != cudaSuccess) return fail(e);
+  if (v) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) return fail(e);
+  }
+  *status = v;
+  return 0;
+}
+
+}  // extern "C"

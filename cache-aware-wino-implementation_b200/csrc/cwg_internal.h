@@ -1,0 +1,78 @@
+/*
+ * cwg_internal.h -- the thin C boundary between the host code (cwg_host.c,
+ * plain C) and the CUDA translation units.  Not installed; not part of the
+ * public ABI in include/cwg.h.
+ */
+#ifndef CWG_INTERNAL_H
+#define CWG_INTERNAL_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Layouts of the transformed weights U in device memory. */
+enum {
+  CWGK_LAYOUT_FFMA_F32 = 1,  /* fp32 [td*td][C_in][C_out]                         */
+  CWGK_LAYOUT_FFMA_BF16 = 2, /* bf16 [td*td][C_in][C_out]                         */
+  CWGK_LAYOUT_TC_X3 = 3,     /* bf16 hi+lo UMMA blocks (fp32-parity tensor path)  */
+  CWGK_LAYOUT_TC_X1 = 4      /* bf16 UMMA blocks (single product)                 */
+};
+
+/* One compiled FFMA kernel configuration. */
+typedef struct cwgk_ffma_cfg {
+  int m;       /* 2 or 4 */
+  int ty, tx;  /* tiles per CTA along y and x */
+  int kb;      /* output channels per CTA */
+  int cc;      /* input channels per pipeline step */
+  int threads; /* threads per CTA */
+  int smem;    /* dynamic shared memory bytes */
+} cwgk_ffma_cfg;
+
+/* Tensor-core kernel geometry (fixed per build). */
+typedef struct cwgk_tc_cfg {
+  int m;          /* output tile edge (2) */
+  int tiles;      /* output tiles per CTA (MMA N) */
+  int kb;         /* output channels per CTA (MMA M) */
+  int cc;         /* input channels per pipeline stage */
+  int threads;    /* threads per CTA */
+  int smem;       /* dynamic shared memory bytes */
+  int tmem_cols;  /* TMEM columns allocated */
+} cwgk_tc_cfg;
+
+int cwgk_ffma_num_cfgs(void);
+int cwgk_ffma_get_cfg(int idx, cwgk_ffma_cfg *out);
+int cwgk_tc_get_cfg(int x3, cwgk_tc_cfg *out);
+
+/* g (or U_ref when from_ref) -> U in `layout`.  Device pointers. */
+int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m, int layout,
+                          int from_ref, void *stream);
+
+/* FFMA fused convolution with configuration `cfg_idx`. */
+int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
+                   int c_in, int c_out, int h, int w, int bf16, int relu, void *stream);
+
+/* tcgen05 fused convolution (F(2,3); c_in % 16 == 0, c_out % 128 == 0). */
+int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
+                 int c_out, int h, int w, int x3, int bf16, int relu, void *stream);
+
+/* Per-tile kernel on device buffers (reference layouts). */
+int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,
+               int td, void *stream);
+
+/* Reads and clears the device status word (after the caller synchronised). */
+int cwgk_read_clear_status(unsigned *status);
+
+/* Launch counter shared by all translation units. */
+void cwgk_count_launch(void);
+long long cwgk_launches(void);
+
+/* Records the last CUDA error code for the calling thread. */
+void cwgk_set_cuda_error(int err);
+int cwgk_get_cuda_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CWG_INTERNAL_H */

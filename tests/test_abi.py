@@ -1,0 +1,144 @@
+"""CPU-side checks of the C ABI: the library loads, exports every symbol the
+header declares, and its host logic (selector, argument checks, error codes)
+behaves -- none of this launches a kernel."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+import cwg
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "cwg.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"\b([a-z_][a-z0-9_]*)\s*\([^;{]*\)\s*;", text)
+    return sorted(set(n for n in names if n not in ("sizeof",)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = cwg.lib()
+    names = declared_functions()
+    assert "fused_winograd_f23" in names and "cwg_conv3x3_fused" in names
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    assert set(cwg.EXPORTED) <= set(names)
+
+
+def test_reference_symbol_signature_is_exported_verbatim():
+    # fused_winograd.c:103-108: void fused_winograd_f23(const float*, const float*, float*, int, int)
+    text = open(HEADER).read()
+    assert re.search(r"void\s+fused_winograd_f23\s*\(\s*const float \*input,\s*const float \*U,"
+                     r"\s*float \*output,\s*int c_in,\s*int c_out\s*\)", text)
+
+
+def test_version_and_strerror():
+    assert "sm_100a" in cwg.version()
+    assert cwg.strerror(cwg.EINVAL) == "invalid argument"
+    assert cwg.strerror(cwg.ETIMEOUT).startswith("device-side wait")
+    assert cwg.strerror(12345) == "unknown status"
+
+
+def test_selector_small_channels_take_ffma():
+    ch = cwg.select(1, 32, 32, 56, 56)
+    assert ch.path == cwg.PATH_FFMA and ch.m == 2
+    assert ch.smem_bytes <= 227 * 1024 and ch.tmem_cols == 0
+    assert ch.gemm_flops == 2 * 28 * 28 * 32 * 32 * 16
+    # bytes: x + y + U + bias
+    assert ch.alg_bytes == 32 * 56 * 56 * 4 * 2 + 16 * 32 * 32 * 4 + 4 * 32
+
+
+def test_selector_auto_m_and_bf16():
+    assert cwg.select(1, 16, 32, 56, 56, 0, cwg.BF16 | cwg.FORCE_FFMA).m == 4
+    assert cwg.select(1, 16, 32, 56, 56, 4).m == 4
+    assert cwg.select(1, 16, 32, 56, 56, 2).m == 2
+
+
+def test_selector_grid_covers_layer():
+    for (n, c, k, h, w, m) in [(1, 32, 32, 56, 56, 2), (3, 16, 17, 7, 5, 4), (2, 64, 64, 1, 1, 2)]:
+        ch = cwg.select(n, c, k, h, w, m, cwg.FORCE_FFMA)
+        th, tw = -(-h // ch.m), -(-w // ch.m)
+        side = int(round(ch.tiles_per_cta ** 0.5))
+        assert ch.ctas == n * (-(-th // side)) * (-(-tw // side)) * (-(-k // ch.cout_per_cta))
+
+
+@pytest.mark.parametrize("args,status", [
+    ((1, 0, 32, 56, 56, 2, 0), cwg.EINVAL),
+    ((1, 32, 0, 56, 56, 2, 0), cwg.EINVAL),
+    ((1, 32, 32, 0, 56, 2, 0), cwg.EINVAL),
+    ((1, 32, 32, 56, 56, 3, 0), cwg.EINVAL),
+    ((1, 32, 32, 56, 56, 6, 0), cwg.EUNSUPPORTED),
+    ((1, 32, 32, 56, 56, 2, cwg.FORCE_FFMA | cwg.FORCE_TC), cwg.EINVAL),
+])
+def test_selector_rejects(args, status):
+    with pytest.raises(cwg.CwgError) as e:
+        cwg.select(*args)
+    assert e.value.status == status
+
+
+def test_weight_bytes():
+    assert cwg.weight_bytes(32, 32, 2, cwg.FORCE_FFMA) == 16 * 32 * 32 * 4
+    assert cwg.weight_bytes(32, 32, 4, cwg.FORCE_FFMA | cwg.BF16) == 36 * 32 * 32 * 2
+    assert cwg.weight_bytes(0, 32, 2) == 0
+    assert cwg.weight_bytes(32, 32, 6) == 0
+
+
+def test_layer_call_argument_checks_need_no_gpu():
+    L = cwg.lib()
+    # NULL pointers / bad sizes are rejected before any CUDA call
+    assert L.cwg_conv3x3_fused(None, None, None, None, 1, 8, 8, 8, 8, 2, 0, None) == cwg.EINVAL
+    assert L.cwg_conv3x3_fused(None, None, None, None, -1, 8, 8, 8, 8, 2, 0, None) == cwg.EINVAL
+    assert L.cwg_conv3x3_fused(None, None, None, None, 0, 8, 8, 8, 8, 2, 0, None) == cwg.OK
+    # misaligned device pointers (checked on the host)
+    assert L.cwg_conv3x3_fused(0x1001, 0x2000, None, 0x3000, 1, 8, 8, 8, 8, 2, 0,
+                               None) == cwg.EINVAL
+    assert L.cwg_weight_transform(None, None, 8, 8, 2, 0, None) == cwg.EINVAL
+    assert L.cwg_weight_import(0x1000, 0x2000, 8, 8, 0, 0, None) == cwg.EINVAL
+    assert L.cwg_conv3x3_fused_host(None, None, None, None, None, 0, 1, 8, 8, 8, 8, 2, 0,
+                                    None) == cwg.EINVAL
+    assert cwg.host_workspace_bytes(2, 3, 4, 5, 6) == 768 + 1024  # 720 B, 960 B, 256-aligned
+    assert cwg.host_workspace_bytes(1, 64, 64, 56, 56) == 2 * 64 * 56 * 56 * 4
+
+
+def test_tiles_argument_checks_need_no_gpu():
+    L = cwg.lib()
+    fp = ctypes.POINTER(ctypes.c_float)
+    a = np.zeros(64, np.float32).ctypes.data_as(fp)
+    assert L.cwg_tiles_fused(a, a, a, 1, 1, 1, 5) == cwg.EINVAL
+    assert L.cwg_tiles_fused(a, a, a, 1, 0, 1, 4) == cwg.EINVAL
+    assert L.cwg_tiles_fused(None, None, None, 1, 1, 1, 4) == cwg.EINVAL
+    assert L.cwg_tiles_fused(None, None, None, 0, 1, 1, 4) == cwg.OK
+    assert L.cwg_last_status() == cwg.OK
+
+
+def test_fused_winograd_kernel_mirror_rejects_bad_td():
+    from fused_winograd_kernel import FusedWinogradKernel, _TRANSFORMS
+
+    k = FusedWinogradKernel(trace_file=None)
+    with pytest.raises(ValueError):
+        k.run_fused(np.zeros((2, 5, 5), np.float32), np.zeros((3, 2, 5, 5), np.float32))
+    assert sorted(_TRANSFORMS) == [4, 6, 8]
+    assert k.BT.shape == (4, 4) and k.AT.shape == (2, 4)
+
+
+def test_mirror_tables_equal_reference_values():
+    from fused_winograd_kernel import _TRANSFORMS
+    from conftest import load_golden  # noqa: F401  (tables are checked numerically below)
+
+    # Bt and At must turn a 3x3 correlation into Winograd form with the derived G
+    G = {4: np.array([[1, 0, 0], [.5, .5, .5], [.5, -.5, .5], [0, 0, 1]]),
+         6: np.array([[1 / 4, 0, 0], [-1 / 6, -1 / 6, -1 / 6], [-1 / 6, 1 / 6, -1 / 6],
+                      [1 / 24, 1 / 12, 1 / 6], [1 / 24, -1 / 12, 1 / 6], [0, 0, 1]])}
+    for td, Gm in G.items():
+        BT, AT = (t.astype(np.float64) for t in _TRANSFORMS[td])
+        m = td - 2
+        for i in range(m):
+            for k in range(3):
+                for j in range(td):
+                    s = sum(AT[i, f] * Gm[f, k] * BT[f, j] for f in range(td))
+                    assert abs(s - (1.0 if j == i + k else 0.0)) < 1e-12

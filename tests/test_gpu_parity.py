@@ -1,0 +1,300 @@
+"""GPU parity: the CUDA path (through the C ABI) against the oracle.
+
+fp32 F(2,3): max abs <= 1e-4 and normwise rel <= 1e-3 against the reference's
+own C kernel (compiled from source) driven over the layer; fp32 F(4,3): the
+same abs bar and rel <= 5e-3 against the C restatement of run_fused; bf16:
+normwise rel <= 1e-2 against an fp64 direct convolution of the bf16-rounded
+inputs and weights.  (Tolerances live in conftest.TOL.)
+"""
+import numpy as np
+import pytest
+
+import cwg
+import oracle
+import workloads
+from conftest import assert_close, load_golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(a, dev, dtype=None):
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return t if dtype is None else t.to(dtype)
+
+
+def make_U(g, c, k, m, flags, dev, U_ref=None):
+    import torch
+
+    U = torch.empty(cwg.weight_bytes(c, k, m, flags), dtype=torch.uint8, device=dev)
+    if U_ref is not None:
+        cwg.weight_import(_t(U_ref, dev), U, c, k, m, flags)
+    else:
+        cwg.weight_transform(_t(g, dev), U, c, k, m, flags)
+    return U
+
+
+def gpu_conv(x, g, bias, m, flags, dev, U_ref=None, U=None):
+    import torch
+
+    n, c, h, w = x.shape
+    k = g.shape[0] if g is not None else U_ref.shape[0]
+    bf = bool(flags & cwg.BF16)
+    dt = torch.bfloat16 if bf else torch.float32
+    x_d = _t(x, dev, dt)
+    if U is None:
+        U = make_U(g, c, k, m, flags, dev, U_ref)
+    b_d = None if bias is None else _t(bias, dev)
+    y_d = torch.full((n, k, h, w), float("nan"), dtype=dt, device=dev)
+    cwg.conv3x3_fused(x_d, U, b_d, y_d, n, c, k, h, w, m, flags)
+    cwg.device_status()
+    return y_d.float().cpu().numpy()
+
+
+def oracle_conv(x, g, bias, m, relu):
+    """Reference C for F(2,3) (when built), C restatement for F(4,3)."""
+    td = m + 2
+    U = oracle.weight_transform(g, td)
+    if m == 2 and oracle.ref_available():
+        return oracle.ref_conv_layer_f23(x, U, bias, relu)
+    return oracle.conv_layer(x, U, bias, td, relu)
+
+
+# ---- per-tile entry points ------------------------------------------------------
+@pytest.mark.parametrize("td", [4, 6, 8])
+def test_tiles_api_vs_reference_run_fused(cuda_dev, td):
+    z = load_golden(f"tiles_td{td}.npz")
+    i = 0
+    while f"tiles_{i}" in z:
+        got = cwg.tiles_fused(z[f"tiles_{i}"], z[f"U_{i}"])
+        ref = z[f"run_fused_{i}"]
+        err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
+        assert err < (1e-5 if td == 8 else 2e-6), (td, i, err)
+        if td == 4:  # same operation order as the reference C: bit-identical
+            np.testing.assert_array_equal(got, z[f"ref_c_{i}"])
+        i += 1
+
+
+def test_fused_winograd_f23_symbol_bit_exact(cuda_dev):
+    z = load_golden("tiles_td4.npz")
+    for i in range(2):
+        for t in range(z[f"tiles_{i}"].shape[0]):
+            out = cwg.fused_winograd_f23(z[f"tiles_{i}"][t], z[f"U_{i}"])
+            np.testing.assert_array_equal(out, z[f"ref_c_{i}"][t])
+
+
+def test_reference_class_mirror(cuda_dev, tmp_path):
+    from fused_winograd_kernel import FusedWinogradKernel
+
+    k = FusedWinogradKernel(trace_file=str(tmp_path / "trace.json"))
+    for td in (4, 6, 8):
+        z = load_golden(f"tiles_td{td}.npz")
+        tiles, U = z["tiles_0"], z["U_0"]
+        for t in range(tiles.shape[0]):
+            for fn, key in ((k.run_fused, "run_fused_0"), (k.run_non_fused, "run_non_fused_0")):
+                y = fn(tiles[t], U)
+                assert y.shape == z[key][t].shape
+                np.testing.assert_allclose(y, z[key][t], rtol=1e-5, atol=1e-5)
+        # batched form
+        np.testing.assert_allclose(k.run_fused(tiles, U), z["run_fused_0"], rtol=1e-5, atol=1e-5)
+    assert (tmp_path / "trace.json").exists()
+
+
+def test_reference_class_conv2d(cuda_dev):
+    from fused_winograd_kernel import FusedWinogradKernel
+
+    z = load_golden("layer_f23_wide.npz")
+    y = FusedWinogradKernel(trace_file=None).conv2d(z["x"], z["g"], z["bias"], m=2, relu=True)
+    assert_close(y, z["y"], "f23", "conv2d")
+
+
+# ---- layer API against the goldens --------------------------------------------
+@pytest.mark.parametrize("name", ["f23_odd", "f23_pixel", "f23_wide", "f43_odd", "f43_small"])
+@pytest.mark.parametrize("how", ["import", "transform"])
+def test_layer_goldens(cuda_dev, name, how):
+    z = load_golden(f"layer_{name}.npz")
+    N, C, K, H, W, td, relu, _ = (int(v) for v in z["meta"])
+    m = td - 2
+    flags = cwg.RELU if relu else 0
+    bias = z.get("bias")
+    y = gpu_conv(z["x"], z["g"], bias, m, flags, cuda_dev,
+                 U_ref=z["U"] if how == "import" else None)
+    assert_close(y, z["y"], "f23" if m == 2 else "f43", name)
+
+
+def test_layer_f63_is_unsupported(cuda_dev):
+    with pytest.raises(cwg.CwgError) as e:
+        cwg.weight_bytes(8, 8, 6) or cwg.select(1, 8, 8, 8, 8, 6)
+    assert e.value.status == cwg.EUNSUPPORTED
+
+
+# ---- the benchmark configurations -----------------------------------------------
+def _run_cfg_layer(layer, dev, n=None):
+    g, bias = workloads.make_weights(layer)
+    x = workloads.make_input(layer, n)
+    flags = (cwg.RELU if layer.relu else 0) | (cwg.BF16 if layer.bf16 else 0)
+    y = gpu_conv(x, g, bias, layer.m, flags, dev)
+    return x, g, bias, y
+
+
+def test_config1(cuda_dev):
+    (layer,) = workloads.config_layers(1)
+    x, g, bias, y = _run_cfg_layer(layer, cuda_dev)
+    assert_close(y, oracle_conv(x, g, bias, 2, layer.relu), "f23", layer.name)
+
+
+@pytest.mark.parametrize("idx", range(14))
+def test_config2_channel_sweep(cuda_dev, idx):
+    layer = workloads.config_layers(2)[idx]
+    x, g, bias, y = _run_cfg_layer(layer, cuda_dev)
+    ref = oracle_conv(x, g, bias, layer.m, layer.relu)
+    assert_close(y, ref, "f23" if layer.m == 2 else "f43", layer.name)
+
+
+def test_config3_full_batch(cuda_dev):
+    (layer,) = workloads.config_layers(3)
+    x, g, bias, y = _run_cfg_layer(layer, cuda_dev)
+    assert_close(y, oracle_conv(x, g, bias, 2, True), "f23", layer.name)
+
+
+def test_config4_resnet18_stack(cuda_dev):
+    """Layers chain within a stage; images 0 and N-1 of every layer are checked
+    against the reference C on the very inputs the GPU layer received."""
+    import torch
+
+    layers = workloads.config_layers(4)
+    sample = [0, layers[0].n - 1]
+    prev_stage = None
+    for layer in layers:
+        g, bias = workloads.make_weights(layer)
+        flags = cwg.RELU
+        if layer.c_in != prev_stage:
+            x_d = _t(workloads.make_input(layer), cuda_dev)
+            prev_stage = layer.c_in
+        n, c, h, w = x_d.shape
+        U = make_U(g, c, layer.c_out, 2, flags, cuda_dev)
+        y_d = torch.empty((n, layer.c_out, h, w), dtype=torch.float32, device=cuda_dev)
+        cwg.conv3x3_fused(x_d, U, _t(bias, cuda_dev), y_d, n, c, layer.c_out, h, w, 2, flags)
+        cwg.device_status()
+        xs = x_d[sample].cpu().numpy()
+        ys = y_d[sample].cpu().numpy()
+        assert_close(ys, oracle_conv(xs, g, bias, 2, True), "f23", layer.name)
+        x_d = y_d
+
+
+def test_config5_bf16_sampled(cuda_dev):
+    (layer,) = workloads.config_layers(5)
+    g, bias = workloads.make_weights(layer)
+    x = workloads.make_input(layer)
+    flags = cwg.RELU | cwg.BF16
+    y = gpu_conv(x, g, bias, layer.m, flags, cuda_dev)
+    for i in (0, layer.n - 1):
+        ref = oracle.direct_conv_f64(x[i:i + 1], g, bias, True)
+        assert_close(y[i:i + 1], ref, "bf16", f"{layer.name} image {i}")
+
+
+# ---- edge cases ---------------------------------------------------------------
+EDGE = [
+    # n, c, k, h, w, m, relu, bias
+    (1, 1, 1, 1, 1, 2, False, False),
+    (1, 1, 1, 1, 1, 4, True, True),
+    (2, 3, 5, 3, 3, 2, True, True),
+    (1, 3, 5, 5, 7, 4, False, True),
+    (3, 7, 17, 7, 7, 2, False, True),
+    (1, 9, 33, 9, 13, 4, True, False),
+    (2, 16, 65, 6, 6, 2, True, True),
+    (1, 17, 16, 31, 2, 2, False, True),
+    (1, 40, 24, 2, 31, 4, True, True),
+    (1, 128, 128, 1, 1, 2, False, True),
+    (1, 64, 64, 3, 3, 2, True, True),
+    (1, 96, 128, 10, 10, 2, True, True),
+    (5, 128, 256, 7, 7, 2, True, True),
+    (1, 48, 192, 9, 15, 2, False, True),
+]
+
+
+@pytest.mark.parametrize("case", EDGE, ids=lambda c: "x".join(map(str, c[:6])))
+def test_edge_shapes(cuda_dev, case):
+    n, c, k, h, w, m, relu, use_bias = case
+    rng = np.random.default_rng(hash(case) % 2 ** 32)
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32) if use_bias else None
+    y = gpu_conv(x, g, bias, m, cwg.RELU if relu else 0, cuda_dev)
+    assert_close(y, oracle_conv(x, g, bias, m, relu), "f23" if m == 2 else "f43", str(case))
+
+
+@pytest.mark.parametrize("force", [cwg.FORCE_FFMA, 0])
+@pytest.mark.parametrize("case", [(2, 32, 64, 9, 11, 2), (1, 64, 128, 12, 12, 4),
+                                  (2, 128, 128, 14, 14, 2)])
+def test_bf16_layers(cuda_dev, case, force):
+    n, c, k, h, w, m = case
+    rng = np.random.default_rng(11)
+    x = workloads.bf16_round(rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32))
+    g = workloads.bf16_round(rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32))
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    flags = cwg.BF16 | cwg.RELU | force
+    try:
+        y = gpu_conv(x, g, bias, m, flags, cuda_dev)
+    except cwg.CwgError as e:
+        assert e.status == cwg.EUNSUPPORTED and force == 0
+        return
+    assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", str(case))
+
+
+def test_paths_agree(cuda_dev):
+    """The FFMA and tensor-core kernels agree on a layer both can run."""
+    rng = np.random.default_rng(12)
+    n, c, k, h, w = 2, 128, 128, 20, 18
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    ref = oracle_conv(x, g, bias, 2, True)
+    for force in (cwg.FORCE_FFMA, cwg.FORCE_TC):
+        try:
+            y = gpu_conv(x, g, bias, 2, cwg.RELU | force, cuda_dev)
+        except cwg.CwgError as e:
+            assert e.status == cwg.EUNSUPPORTED and force == cwg.FORCE_TC
+            continue
+        assert_close(y, ref, "f23", f"force={force:#x}")
+
+
+def test_host_buffer_entry_matches_device_entry(cuda_dev):
+    import torch
+
+    rng = np.random.default_rng(13)
+    n, c, k, h, w, m = 2, 32, 48, 15, 17, 2
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, 0.1, (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    U = make_U(g, c, k, m, cwg.RELU, cuda_dev)
+    y_dev = gpu_conv(x, g, bias, m, cwg.RELU, cuda_dev, U=U)
+    ws_b = cwg.host_workspace_bytes(n, c, k, h, w)
+    ws = torch.empty(ws_b, dtype=torch.uint8, device=cuda_dev)
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.empty((n, k, h, w), dtype=torch.float32).pin_memory()
+    cwg.conv3x3_fused_host(int(xh.data_ptr()), U, _t(bias, cuda_dev), int(yh.data_ptr()), ws,
+                           ws_b, n, c, k, h, w, m, cwg.RELU)
+    np.testing.assert_array_equal(yh.numpy(), y_dev)
+
+
+def test_errors_and_launch_counter(cuda_dev):
+    import torch
+
+    before = cwg.launch_count()
+    rng = np.random.default_rng(14)
+    x = rng.uniform(-1, 1, (1, 8, 8, 8)).astype(np.float32)
+    g = rng.normal(0, 0.1, (8, 8, 3, 3)).astype(np.float32)
+    gpu_conv(x, g, None, 2, 0, cuda_dev)
+    assert cwg.launch_count() >= before + 2  # weight transform + conv
+    U = make_U(g, 8, 8, 2, 0, cuda_dev)
+    x_d = _t(x, cuda_dev)
+    y_d = torch.empty((1, 8, 8, 8), device=cuda_dev)
+    with pytest.raises(cwg.CwgError) as e:  # misaligned output pointer
+        cwg.conv3x3_fused(x_d, U, None, int(y_d.data_ptr()) + 2, 1, 8, 8, 8, 8, 2, 0)
+    assert e.value.status == cwg.EINVAL
+    with pytest.raises(cwg.CwgError) as e:
+        cwg.conv3x3_fused(x_d, U, None, y_d, 1, 8, 8, 8, 8, 6, 0)
+    assert e.value.status == cwg.EUNSUPPORTED
+    cwg.device_status()
