@@ -12,10 +12,6 @@
 
 namespace cwg {
 
-// Device-side status word.  Bounded waits in the tensor-core kernel set bit 0
-// when they give up; cwg_device_status() reads and clears it.
-__device__ unsigned int g_status;
-
 static std::atomic<long long> g_launches{0};
 static thread_local int t_cuda_error = 0;
 
@@ -74,8 +70,8 @@ __device__ __forceinline__ void transform_one(const float *src, int from_ref, fl
 }
 
 // One thread per (c, k); k fastest so the [f][C][K] stores coalesce.
-template <int M, typename Tu>
-__global__ void wt_transform_ffma(const float *__restrict__ src, Tu *__restrict__ U, int C,
+template <int M>
+__global__ void wt_transform_ffma(const float *__restrict__ src, float *__restrict__ U, int C,
                                   int K, int from_ref) {
   constexpr int NF = (M + 2) * (M + 2);
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -84,7 +80,7 @@ __global__ void wt_transform_ffma(const float *__restrict__ src, Tu *__restrict_
   float u[NF];
   transform_one<M>(src + ((long)k * C + c) * (from_ref ? NF : 9), from_ref, u);
 #pragma unroll
-  for (int f = 0; f < NF; ++f) U[((long)f * C + c) * K + k] = from_f32<Tu>(u[f]);
+  for (int f = 0; f < NF; ++f) U[((long)f * C + c) * K + k] = u[f];
 }
 
 // ============================================================================
@@ -132,7 +128,7 @@ __device__ __forceinline__ void lds_vec(const float *p, float (&v)[N]) {
 
 template <int M, int TY, int TX, int KB, int CC, int FPW, typename Tio>
 __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
-    wino_fused_ffma(const Tio *__restrict__ x, const Tio *__restrict__ U,
+    wino_fused_ffma(const Tio *__restrict__ x, const float *__restrict__ U,
                     const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
                     int W, int tiles_y, int tiles_x, int relu) {
   using G = FG<M, TY, TX, KB, CC, FPW>;
@@ -175,7 +171,7 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
     for (int i = tid; i < G::US; i += NT) {
       const int k = i % KB, fc = i / KB, c = fc % CC, f = fc / CC;
       float v = 0.f;
-      if (c0 + c < C && k0 + k < K) v = to_f32(U[((size_t)f * C + c0 + c) * K + k0 + k]);
+      if (c0 + c < C && k0 + k < K) v = U[((size_t)f * C + c0 + c) * K + k0 + k];
       us[i] = v;
     }
     __syncthreads();
@@ -371,29 +367,18 @@ int cwgk_ffma_get_cfg(int idx, cwgk_ffma_cfg *out) {
 
 int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m, int layout,
                           int from_ref, void *stream) {
-  if (layout != CWGK_LAYOUT_FFMA_F32 && layout != CWGK_LAYOUT_FFMA_BF16) return -2;
+  if (layout != CWGK_LAYOUT_FFMA_F32) return cwgk_weight_transform_tc(src, U, c_in, c_out, m,
+                                                                      layout, from_ref, stream);
   const long total = (long)c_in * c_out;
   const int threads = 256;
   const unsigned blocks = (unsigned)((total + threads - 1) / threads);
   cudaStream_t s = (cudaStream_t)stream;
-  const bool bf = layout == CWGK_LAYOUT_FFMA_BF16;
-  if (m == 2) {
-    if (bf)
-      wt_transform_ffma<2, __nv_bfloat16>
-          <<<blocks, threads, 0, s>>>(src, (__nv_bfloat16 *)U, c_in, c_out, from_ref);
-    else
-      wt_transform_ffma<2, float><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out,
-                                                             from_ref);
-  } else if (m == 4) {
-    if (bf)
-      wt_transform_ffma<4, __nv_bfloat16>
-          <<<blocks, threads, 0, s>>>(src, (__nv_bfloat16 *)U, c_in, c_out, from_ref);
-    else
-      wt_transform_ffma<4, float><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out,
-                                                             from_ref);
-  } else {
+  if (m == 2)
+    wt_transform_ffma<2><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out, from_ref);
+  else if (m == 4)
+    wt_transform_ffma<4><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out, from_ref);
+  else
     return -2;
-  }
   cwgk_count_launch();
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : fail(e);
@@ -437,19 +422,6 @@ int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int 
   cwgk_count_launch();
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? 0 : fail(e);
-}
-
-int cwgk_read_clear_status(unsigned *status) {
-  unsigned v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
-  if (e != cudaSuccess) return fail(e);
-  if (v) {
-    const unsigned zero = 0;
-    e = cudaMemcpyToSymbol(g_status, &zero, sizeof(zero));
-    if (e != cudaSuccess) return fail(e);
-  }
-  *status = v;
-  return 0;
 }
 
 }  // extern "C"

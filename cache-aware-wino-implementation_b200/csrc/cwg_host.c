@@ -83,9 +83,9 @@ static int tc_available(int x3) {
   return cwgk_tc_get_cfg(x3, &cfg) == 0;
 }
 
-static int tc_shape_ok(int c_in, int c_out) {
-  return c_in >= 32 && (c_in % 16) == 0 && c_out >= 64 && (c_out % 64) == 0;
-}
+/* Tensor cores only where the per-frequency GEMM is a real contraction: both
+ * channel counts >= 64 (the kernel zero-pads C_in to 16 and C_out to 128). */
+static int tc_shape_ok(int c_in, int c_out) { return c_in >= 64 && c_out >= 64; }
 
 /* Resolves m and the path; returns CWG_OK or an error. */
 static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *path_out) {
@@ -117,14 +117,15 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
 static int layout_of(int path, unsigned flags) {
   if (path == CWG_PATH_TC)
     return (flags & (CWG_BF16 | CWG_TC_SINGLE)) ? CWGK_LAYOUT_TC_X1 : CWGK_LAYOUT_TC_X3;
-  return (flags & CWG_BF16) ? CWGK_LAYOUT_FFMA_BF16 : CWGK_LAYOUT_FFMA_F32;
+  /* The CUDA-core kernel keeps U in fp32 for bf16 layers too: rounding U to
+   * bf16 loses ~4% through F(4,3)'s output transform (coefficients up to 8). */
+  return CWGK_LAYOUT_FFMA_F32;
 }
 
 static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
   const size_t nf = (size_t)(m + 2) * (m + 2);
   switch (layout) {
     case CWGK_LAYOUT_FFMA_F32: return nf * c_in * c_out * 4;
-    case CWGK_LAYOUT_FFMA_BF16: return nf * c_in * c_out * 2;
     case CWGK_LAYOUT_TC_X3:
     case CWGK_LAYOUT_TC_X1: {
       const size_t kp = ((size_t)c_out + 127) / 128 * 128;

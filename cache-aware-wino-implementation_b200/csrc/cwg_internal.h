@@ -14,8 +14,7 @@ extern "C" {
 
 /* Layouts of the transformed weights U in device memory. */
 enum {
-  CWGK_LAYOUT_FFMA_F32 = 1,  /* fp32 [td*td][C_in][C_out]                         */
-  CWGK_LAYOUT_FFMA_BF16 = 2, /* bf16 [td*td][C_in][C_out]                         */
+  CWGK_LAYOUT_FFMA_F32 = 1,  /* fp32 [td*td][C_in][C_out] (fp32 and bf16 layers)  */
   CWGK_LAYOUT_TC_X3 = 3,     /* bf16 hi+lo UMMA blocks (fp32-parity tensor path)  */
   CWGK_LAYOUT_TC_X1 = 4      /* bf16 UMMA blocks (single product)                 */
 };
@@ -48,6 +47,10 @@ int cwgk_tc_get_cfg(int x3, cwgk_tc_cfg *out);
 /* g (or U_ref when from_ref) -> U in `layout`.  Device pointers. */
 int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m, int layout,
                           int from_ref, void *stream);
+
+/* Tensor-core weight layouts (CWGK_LAYOUT_TC_*), defined with the tcgen05 kernel. */
+int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int m, int layout,
+                             int from_ref, void *stream);
 
 /* FFMA fused convolution with configuration `cfg_idx`. */
 int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,

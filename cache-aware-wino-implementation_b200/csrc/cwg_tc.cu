@@ -1,19 +1,606 @@
-// cwg_tc.cu -- tcgen05/TMEM fused Winograd kernel (placeholder until the
-// tensor-core path lands: reports "not available" so the selector keeps every
-// layer on the FFMA kernel).
-#include "cwg_internal.h"
+// cwg_tc.cu -- the tcgen05/TMEM fused Winograd F(2x2,3x3) kernel (sm_100a).
+//
+// One CTA computes 128 output channels x 32 output tiles (2x2 pixels each) of
+// one layer:
+//   * A = U_f   (128 output channels x 16 input channels, bf16, K-major), one
+//                per Winograd frequency f, streamed from global memory by
+//                cp.async.bulk (the weight transform already wrote each
+//                (channel block, 16-channel step, frequency) as the exact
+//                shared-memory image the tensor core reads);
+//   * B = V_f   (32 tiles x 16 input channels, bf16, K-major), written into
+//                shared memory by four transform warps that load the 4x4 input
+//                patches from global memory and compute Bt d B in registers;
+//   * D_f in TMEM: the 16 frequency accumulators (128 lanes x 32 columns each)
+//                fill all 512 columns, so the whole C_in reduction of every
+//                frequency completes on chip;
+//   * epilogue: the same four warps read D (lane = output channel) with
+//                tcgen05.ld, apply At M A, bias and ReLU, and store NCHW.
+// fp32 parity ("x3"): every fp32 operand v is split into hi = bf16(v) and
+// lo = bf16(v - hi); each product runs as three MMAs (hi*hi + hi*lo + lo*hi)
+// into the same fp32 accumulator.  "x1" (bf16 layers) runs one MMA.
+//
+// Warp roles (192 threads): warp 0 allocates TMEM and issues the MMAs from one
+// thread; warp 1 issues the bulk copies of U; warps 2-5 transform and run the
+// epilogue.  Every mbarrier wait is bounded by %globaltimer: on timeout the
+// kernel sets g_tc_status, drains what it has in flight, frees TMEM and
+// returns, and the host reports CWG_ETIMEOUT.
+#include <cstdint>
+
+#include "cwg_common.cuh"
+
+namespace cwg {
+namespace tc {
+
+constexpr int kTiles = 32;     // MMA N
+constexpr int kCout = 128;     // MMA M
+constexpr int kCc = 16;        // input channels per pipeline stage (one MMA K step)
+constexpr int kNF = 16;        // frequencies of F(2,3)
+constexpr int kFPerU = 2;      // frequencies per U stage
+constexpr int kNV = 2;         // V stages
+constexpr int kNU = 3;         // U stages
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kCoreBytes = 4096;               // one 128x16 bf16 operand block
+constexpr int kVBytes = kTiles * kCc * 2;      // one 32x16 bf16 operand block (1 KiB)
+constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
+
+template <bool X3>
+struct Layout {
+  static constexpr int kParts = X3 ? 2 : 1;                       // hi (+ lo)
+  static constexpr int kVStage = kParts * kNF * kVBytes;          // 16 or 32 KiB
+  static constexpr int kUStage = kFPerU * kParts * kCoreBytes;    // 8 or 16 KiB
+  static constexpr int kVOff = 0;
+  static constexpr int kUOff = kVOff + kNV * kVStage;
+  static constexpr int kBarOff = kUOff + kNU * kUStage;
+  // barriers: v_full[kNV], v_empty[kNV], u_full[kNU], u_empty[kNU], acc_full, drain
+  static constexpr int kNumBars = 2 * kNV + 2 * kNU + 2;
+  static constexpr int kTmemSlot = kBarOff + 8 * kNumBars;
+  static constexpr int kAbortSlot = kTmemSlot + 4;
+  static constexpr int kSmem = kAbortSlot + 4;
+};
+
+__device__ unsigned int g_tc_status;
+
+// ---- PTX wrappers -------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+      "r"(bytes)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: true when the phase completed; false on timeout or when another
+// role already aborted (the abort flag lives in shared memory).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > kTimeoutNs) {
+      *abort = 1;
+      atomicOr(&g_tc_status, 1u);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::
+                   "r"(bar)
+               : "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, bf16 x bf16 -> fp32.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {
+  uint32_t r0, r1, r2, r3;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(taddr)
+               : "memory");
+  v[0] = __uint_as_float(r0);
+  v[1] = __uint_as_float(r1);
+  v[2] = __uint_as_float(r2);
+  v[3] = __uint_as_float(r3);
+}
+// Named barrier 1: TMEM address handoff from warp 0 to the epilogue warps.
+constexpr int kBarTmem = 1;
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, no swizzle.  Core matrices are
+// 8 rows x 16 bytes; `lbo` = byte distance between the two K-adjacent core
+// matrices of one MMA step, `sbo` = byte distance between 8-row groups.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  return d;                // base offset 0, legacy LBO mode, SWIZZLE_NONE
+}
+
+// Instruction descriptor: kind::f16, A = B = bf16, D = fp32, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
+  return (1u << 4)                     // D format fp32
+         | (1u << 7)                   // A format bf16
+         | (1u << 10)                  // B format bf16
+         | ((uint32_t)(n >> 3) << 17)  // N / 8
+         | ((uint32_t)(m >> 4) << 24); // M / 16
+}
+
+// Byte offset of element (row, k) inside one K-major no-swizzle operand block
+// of 16 K-elements: 8-row groups 256 B apart, K halves 128 B apart.
+__host__ __device__ constexpr uint32_t blk_off(int row, int k) {
+  return (uint32_t)((row >> 3) * 256 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
+  // element with the lower k index goes to the lower half
+  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo_elem));
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi_elem));
+  return a | (b << 16);
+}
+
+// ---- weight transform into UMMA blocks ------------------------------------------
+// U layout: [K_pad/128][C_pad/16][16 f][parts][4096 B block], block element
+// (k % 128, c % 16) at blk_off.  Channels past C_out / C_in are zero.
+template <bool X3>
+__global__ void wt_transform_tc(const float *__restrict__ src, uint8_t *__restrict__ U, int C,
+                                int K, int Cp, int Kp, int from_ref) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)Cp * Kp) return;
+  const int c = (int)(idx % Cp), k = (int)(idx / Cp);
+  float u[kNF];
+  if (k < K && c < C) {
+    if (from_ref) {
+#pragma unroll
+      for (int f = 0; f < kNF; ++f) u[f] = src[((long)k * C + c) * kNF + f];
+    } else {
+      // fp64 G g G^T, same operation order as the CPU oracle, rounded once
+      const double G[4][3] = {{1, 0, 0}, {.5, .5, .5}, {.5, -.5, .5}, {0, 0, 1}};
+      const float *g = src + ((long)k * C + c) * 9;
+      double t[4][3];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          double s = 0.0;
+#pragma unroll
+          for (int i = 0; i < 3; ++i) s = __dadd_rn(s, __dmul_rn(G[a][i], (double)g[i * 3 + j]));
+          t[a][j] = s;
+        }
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          double s = 0.0;
+#pragma unroll
+          for (int j = 0; j < 3; ++j) s = __dadd_rn(s, __dmul_rn(t[a][j], G[b][j]));
+          u[a * 4 + b] = (float)s;
+        }
+    }
+  } else {
+#pragma unroll
+    for (int f = 0; f < kNF; ++f) u[f] = 0.f;
+  }
+  constexpr int parts = X3 ? 2 : 1;
+  const int C16 = Cp / kCc;
+  const long blk0 = (long)(k / kCout) * C16 + c / kCc;
+  const uint32_t off = blk_off(k % kCout, c % kCc);
+#pragma unroll
+  for (int f = 0; f < kNF; ++f) {
+    const __nv_bfloat16 hi = __float2bfloat16_rn(u[f]);
+    uint8_t *b = U + ((blk0 * kNF + f) * parts) * kCoreBytes;
+    *reinterpret_cast<__nv_bfloat16 *>(b + off) = hi;
+    if (X3) {
+      const __nv_bfloat16 lo = __float2bfloat16_rn(u[f] - __bfloat162float(hi));
+      *reinterpret_cast<__nv_bfloat16 *>(b + kCoreBytes + off) = lo;
+    }
+  }
+}
+
+// ---- the fused kernel -------------------------------------------------------------
+template <bool X3, typename Tio>
+__global__ void __launch_bounds__(kThreads, 2)
+    wino_fused_tc(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
+                  const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H, int W,
+                  int tiles_y, int tiles_x, long long total_tiles, int relu) {
+  using L = Layout<X3>;
+  constexpr int P = L::kParts;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t v_full = sbase + L::kBarOff, v_empty = v_full + 8 * kNV;
+  const uint32_t u_full = v_empty + 8 * kNV, u_empty = u_full + 8 * kNU;
+  const uint32_t acc_full = u_empty + 8 * kNU, drain = acc_full + 8;
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + L::kAbortSlot);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kTmemSlot);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int C16 = (C + kCc - 1) / kCc;
+  const int kblk = blockIdx.y;
+  const long long tile0 = (long long)blockIdx.x * kTiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNV; ++i) {
+      mbar_init(v_full + 8 * i, 4);
+      mbar_init(v_empty + 8 * i, 1);
+    }
+    for (int i = 0; i < kNU; ++i) {
+      mbar_init(u_full + 8 * i, 1);
+      mbar_init(u_empty + 8 * i, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ---------------- TMEM owner + MMA issuer ----------------
+    // The allocation may wait for a co-resident CTA to free its columns; the
+    // producer and transform warps meanwhile fill the first stages.
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tc_fence_before();
+    __syncwarp();
+    named_bar_arrive(kBarTmem, 32 + 128);  // hands the address to the epilogue warps
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc(kCout, kTiles);
+      bool ok = true;
+      int ui = 0;
+      for (int cs = 0; cs < C16 && ok; ++cs) {
+        const int vs = cs % kNV;
+        if (!(ok = mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort))) break;
+        tc_fence_after();
+        const uint32_t vbase = sbase + L::kVOff + vs * L::kVStage;
+        for (int fp = 0; fp < kNF / kFPerU; ++fp, ++ui) {
+          const int us = ui % kNU;
+          if (!(ok = mbar_wait(u_full + 8 * us, (ui / kNU) & 1, abort))) break;
+          tc_fence_after();
+          const uint32_t ubase = sbase + L::kUOff + us * L::kUStage;
+#pragma unroll
+          for (int fi = 0; fi < kFPerU; ++fi) {
+            const int f = fp * kFPerU + fi;
+            const uint32_t d = tmem + (uint32_t)(f * kTiles);
+            const uint32_t a_hi = ubase + (fi * P) * kCoreBytes;
+            const uint32_t b_hi = vbase + f * kVBytes;
+            const uint64_t ah = smem_desc(a_hi, 128, 256), bh = smem_desc(b_hi, 128, 256);
+            mma_bf16(d, ah, bh, idesc, cs > 0 ? 1u : 0u);
+            if (X3) {
+              const uint64_t al = smem_desc(a_hi + kCoreBytes, 128, 256);
+              const uint64_t bl = smem_desc(b_hi + kNF * kVBytes, 128, 256);
+              mma_bf16(d, ah, bl, idesc, 1u);
+              mma_bf16(d, al, bh, idesc, 1u);
+            }
+          }
+          tc_commit(u_empty + 8 * us);
+        }
+        if (ok) tc_commit(v_empty + 8 * vs);
+      }
+      if (ok) {
+        tc_commit(acc_full);
+      } else {
+        // drain whatever was issued before giving up
+        tc_commit(drain);
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try(drain, 0) && globaltimer() - t0 < kTimeoutNs) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- producer: U stages by bulk copy ----------------
+    if (lane == 0) {
+      const int nstages = C16 * (kNF / kFPerU);
+      const uint8_t *ublk = U + (size_t)kblk * C16 * kNF * P * kCoreBytes;
+      int issued = 0;
+      for (int i = 0; i < nstages; ++i) {
+        const int s = i % kNU;
+        if (!mbar_wait(u_empty + 8 * s, ((i / kNU) & 1) ^ 1, abort)) break;
+        mbar_expect_tx(u_full + 8 * s, L::kUStage);
+        bulk_g2s(sbase + L::kUOff + s * L::kUStage, ublk + (size_t)i * L::kUStage, L::kUStage,
+                 u_full + 8 * s);
+        issued = i + 1;
+      }
+      // never leave the CTA with a copy still writing shared memory
+      for (int i = issued - kNU > 0 ? issued - kNU : 0; i < issued; ++i) {
+        const int s = i % kNU;
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try(u_full + 8 * s, (i / kNU) & 1) && globaltimer() - t0 < kTimeoutNs) {
+        }
+      }
+    }
+  } else {
+    // ---------------- transform warps, then epilogue ----------------
+    const int tw = warp - 2;            // 0..3
+    const int r = lane >> 2, g = lane & 3;
+    const int t = tw * 8 + r;           // tile within the CTA
+    const long long T = tile0 + t;
+    const bool tile_ok = T < total_tiles;
+    int n = 0, ty = 0, tx = 0;
+    if (tile_ok) {
+      const long long per_img = (long long)tiles_y * tiles_x;
+      n = (int)(T / per_img);
+      const int rem = (int)(T - (long long)n * per_img);
+      ty = rem / tiles_x;
+      tx = rem - ty * tiles_x;
+    }
+    const int y0 = 2 * ty - 1, x0 = 2 * tx - 1;
+    const size_t plane = (size_t)H * W;
+    const Tio *xn = x + (size_t)n * C * plane;
+    // row/column validity of the 4x4 patch (pad = 1)
+    bool rv[4], cv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      rv[i] = tile_ok && (y0 + i) >= 0 && (y0 + i) < H;
+      cv[i] = (x0 + i) >= 0 && (x0 + i) < W;
+    }
+    float d[4][4][4];  // [channel of 4][row][col]
+    auto load_stage = [&](int cs) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int c = cs * kCc + g * 4 + q;
+        const bool cok = c < C;
+        const Tio *xc = xn + (size_t)c * plane;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            d[q][i][j] = (cok && rv[i] && cv[j])
+                             ? to_f32(xc[(size_t)(y0 + i) * W + (x0 + j)])
+                             : 0.f;
+      }
+    };
+    bool ok = true;
+    if (C16 > 0) load_stage(0);
+    for (int cs = 0; cs < C16; ++cs) {
+      const int vs = cs % kNV;
+      ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
+      if (!ok) break;
+      uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
+      const uint32_t off = blk_off(t, g * 4);
+      float v[4][4][4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) input_transform<2>(d[q], v[q]);
+#pragma unroll
+      for (int f = 0; f < kNF; ++f) {
+        const int a = f >> 2, b = f & 3;
+        float e0 = v[0][a][b], e1 = v[1][a][b], e2 = v[2][a][b], e3 = v[3][a][b];
+        uint2 hi;
+        hi.x = pack_bf16(e0, e1);
+        hi.y = pack_bf16(e2, e3);
+        *reinterpret_cast<uint2 *>(vb + f * kVBytes + off) = hi;
+        if (X3) {
+          const float h0 = __bfloat162float(__float2bfloat16_rn(e0));
+          const float h1 = __bfloat162float(__float2bfloat16_rn(e1));
+          const float h2 = __bfloat162float(__float2bfloat16_rn(e2));
+          const float h3 = __bfloat162float(__float2bfloat16_rn(e3));
+          uint2 lo;
+          lo.x = pack_bf16(e0 - h0, e1 - h1);
+          lo.y = pack_bf16(e2 - h2, e3 - h3);
+          *reinterpret_cast<uint2 *>(vb + (kNF + f) * kVBytes + off) = lo;
+        }
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(v_full + 8 * vs);
+      if (cs + 1 < C16) load_stage(cs + 1);
+    }
+
+    // ---------------- epilogue ----------------
+    named_bar_sync(kBarTmem, 32 + 128);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort));
+    tc_fence_after();
+    if (ok) {
+      const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+      const int k = kblk * kCout + quad * 32 + lane;
+      const float bk = (bias != nullptr && k < K) ? bias[k] : 0.f;
+      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+#pragma unroll 1
+      for (int gq = 0; gq < kTiles / 4; ++gq) {
+        float acc[kNF][4];
+#pragma unroll
+        for (int f = 0; f < kNF; ++f) tmem_ld4(trow + (uint32_t)(f * kTiles + gq * 4), acc[f]);
+        tmem_wait_ld();
+        if (k >= K) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const long long TT = tile0 + gq * 4 + j;
+          if (TT >= total_tiles) break;
+          const long long per_img = (long long)tiles_y * tiles_x;
+          const int nn = (int)(TT / per_img);
+          const int rem = (int)(TT - (long long)nn * per_img);
+          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
+          float mm[4][4], o[2][2];
+#pragma unroll
+          for (int f = 0; f < kNF; ++f) mm[f >> 2][f & 3] = acc[f][j];
+          output_transform<2>(mm, o);
+          Tio *yk = y + ((size_t)nn * K + k) * plane;
+#pragma unroll
+          for (int i = 0; i < 2; ++i)
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              const int oy = 2 * yy + i, ox = 2 * xx + jj;
+              if (oy < H && ox < W) {
+                float val = o[i][jj] + bk;
+                if (relu) val = val < 0.f ? 0.f : val;
+                yk[(size_t)oy * W + ox] = from_f32<Tio>(val);
+              }
+            }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot),
+                 "r"(kTmemCols));
+  }
+}
+
+template <bool X3, typename Tio>
+static cudaError_t launch(const void *x, const void *U, const float *bias, void *y, int n, int c,
+                          int k, int h, int w, int relu, cudaStream_t s) {
+  const int tiles_y = (h + 1) / 2, tiles_x = (w + 1) / 2;
+  const long long total = (long long)n * tiles_y * tiles_x;
+  const long long gx = (total + kTiles - 1) / kTiles;
+  const int gy = (k + kCout - 1) / kCout;
+  if (gx > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidValue;
+  auto fn = wino_fused_tc<X3, Tio>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Layout<X3>::kSmem);
+  if (e != cudaSuccess) return e;
+  fn<<<dim3((unsigned)gx, (unsigned)gy), kThreads, Layout<X3>::kSmem, s>>>(
+      (const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y, tiles_x, total,
+      relu);
+  return cudaGetLastError();
+}
+
+}  // namespace tc
+}  // namespace cwg
+
+using namespace cwg;
 
 extern "C" {
 
 int cwgk_tc_get_cfg(int x3, cwgk_tc_cfg *out) {
-  (void)x3;
-  (void)out;
-  return -2;
+  if (!out) return -1;
+  out->m = 2;
+  out->tiles = tc::kTiles;
+  out->kb = tc::kCout;
+  out->cc = tc::kCc;
+  out->threads = tc::kThreads;
+  out->smem = x3 ? tc::Layout<true>::kSmem : tc::Layout<false>::kSmem;
+  out->tmem_cols = tc::kTmemCols;
+  return 0;
 }
 
-int cwgk_conv_tc(const void *, const void *, const float *, void *, int, int, int, int, int, int,
-                 int, int, void *) {
-  return -2;
+int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int m, int layout,
+                             int from_ref, void *stream) {
+  if (m != 2 || (layout != CWGK_LAYOUT_TC_X3 && layout != CWGK_LAYOUT_TC_X1)) return -2;
+  const int Cp = (c_in + tc::kCc - 1) / tc::kCc * tc::kCc;
+  const int Kp = (c_out + tc::kCout - 1) / tc::kCout * tc::kCout;
+  const long total = (long)Cp * Kp;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)((total + threads - 1) / threads);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (layout == CWGK_LAYOUT_TC_X3)
+    tc::wt_transform_tc<true>
+        <<<blocks, threads, 0, s>>>(src, (uint8_t *)U, c_in, c_out, Cp, Kp, from_ref);
+  else
+    tc::wt_transform_tc<false>
+        <<<blocks, threads, 0, s>>>(src, (uint8_t *)U, c_in, c_out, Cp, Kp, from_ref);
+  cwgk_count_launch();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cwgk_set_cuda_error((int)e);
+    return -3;
+  }
+  return 0;
+}
+
+int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
+                 int c_out, int h, int w, int x3, int bf16, int relu, void *stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e;
+  if (x3) {
+    e = bf16 ? tc::launch<true, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s)
+             : tc::launch<true, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s);
+  } else {
+    e = bf16 ? tc::launch<false, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s)
+             : tc::launch<false, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s);
+  }
+  cwgk_count_launch();
+  if (e != cudaSuccess) {
+    cwgk_set_cuda_error((int)e);
+    return -3;
+  }
+  return 0;
+}
+
+int cwgk_read_clear_status(unsigned *status) {
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, tc::g_tc_status, sizeof(v));
+  if (e == cudaSuccess && v) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(tc::g_tc_status, &zero, sizeof(zero));
+  }
+  if (e != cudaSuccess) {
+    cwgk_set_cuda_error((int)e);
+    return -3;
+  }
+  *status = v;
+  return 0;
 }
 
 }  // extern "C"

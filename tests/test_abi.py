@@ -83,7 +83,7 @@ def test_selector_rejects(args, status):
 
 def test_weight_bytes():
     assert cwg.weight_bytes(32, 32, 2, cwg.FORCE_FFMA) == 16 * 32 * 32 * 4
-    assert cwg.weight_bytes(32, 32, 4, cwg.FORCE_FFMA | cwg.BF16) == 36 * 32 * 32 * 2
+    assert cwg.weight_bytes(32, 32, 4, cwg.FORCE_FFMA | cwg.BF16) == 36 * 32 * 32 * 4
     assert cwg.weight_bytes(0, 32, 2) == 0
     assert cwg.weight_bytes(32, 32, 6) == 0
 

@@ -27,7 +27,10 @@ def _t(a, dev, dtype=None):
 def make_U(g, c, k, m, flags, dev, U_ref=None):
     import torch
 
-    U = torch.empty(cwg.weight_bytes(c, k, m, flags), dtype=torch.uint8, device=dev)
+    nbytes = cwg.weight_bytes(c, k, m, flags)
+    if nbytes == 0:  # the selector refuses this layer: raise its status
+        cwg.select(1, c, k, 8, 8, m, flags)
+    U = torch.empty(nbytes, dtype=torch.uint8, device=dev)
     if U_ref is not None:
         cwg.weight_import(_t(U_ref, dev), U, c, k, m, flags)
     else:
@@ -94,10 +97,13 @@ def test_reference_class_mirror(cuda_dev, tmp_path):
         for t in range(tiles.shape[0]):
             for fn, key in ((k.run_fused, "run_fused_0"), (k.run_non_fused, "run_non_fused_0")):
                 y = fn(tiles[t], U)
-                assert y.shape == z[key][t].shape
-                np.testing.assert_allclose(y, z[key][t], rtol=1e-5, atol=1e-5)
+                ref = z[key][t]
+                assert y.shape == ref.shape
+                # normwise: F(6,3)'s coefficients (up to 32) amplify summation order
+                assert np.abs(y - ref).max() / np.abs(ref).max() < (1e-5 if td == 8 else 2e-6)
         # batched form
-        np.testing.assert_allclose(k.run_fused(tiles, U), z["run_fused_0"], rtol=1e-5, atol=1e-5)
+        ref = z["run_fused_0"]
+        assert np.abs(k.run_fused(tiles, U) - ref).max() / np.abs(ref).max() < 1e-5
     assert (tmp_path / "trace.json").exists()
 
 
