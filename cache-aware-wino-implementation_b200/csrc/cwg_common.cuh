@@ -86,6 +86,14 @@ __device__ __forceinline__ float madd(float c, float d, float s) {
   return EXACT ? __fadd_rn(s, __fmul_rn(c, d)) : fmaf(c, d, s);
 }
 
+// Sum of coefficient * value over the nonzero coefficients of one table row,
+// in index order.  The sum starts from the first term itself (a +-1
+// coefficient costs nothing), so only one add per further term remains.
+template <bool EXACT>
+__device__ __forceinline__ float first_term(float c, float d) {
+  return c == 1.f ? d : (c == -1.f ? -d : (EXACT ? __fmul_rn(c, d) : c * d));
+}
+
 // v = Bt d B (td x td, row-major), sequential in the reference's index order.
 template <int M, bool EXACT = false>
 __device__ __forceinline__ void input_transform(const float (&d)[M + 2][M + 2],
@@ -97,9 +105,14 @@ __device__ __forceinline__ void input_transform(const float (&d)[M + 2][M + 2],
 #pragma unroll
     for (int j = 0; j < TD; ++j) {
       float s = 0.f;
+      bool first = true;
 #pragma unroll
-      for (int i = 0; i < TD; ++i)
-        if (Wino<M>::bt(a, i) != 0.f) s = madd<EXACT>(Wino<M>::bt(a, i), d[i][j], s);
+      for (int i = 0; i < TD; ++i) {
+        const float c = Wino<M>::bt(a, i);
+        if (c == 0.f) continue;
+        s = first ? first_term<EXACT>(c, d[i][j]) : madd<EXACT>(c, d[i][j], s);
+        first = false;
+      }
       t[a][j] = s;
     }
 #pragma unroll
@@ -107,9 +120,14 @@ __device__ __forceinline__ void input_transform(const float (&d)[M + 2][M + 2],
 #pragma unroll
     for (int b = 0; b < TD; ++b) {
       float s = 0.f;
+      bool first = true;
 #pragma unroll
-      for (int j = 0; j < TD; ++j)
-        if (Wino<M>::bt(b, j) != 0.f) s = madd<EXACT>(Wino<M>::bt(b, j), t[a][j], s);
+      for (int j = 0; j < TD; ++j) {
+        const float c = Wino<M>::bt(b, j);
+        if (c == 0.f) continue;
+        s = first ? first_term<EXACT>(c, t[a][j]) : madd<EXACT>(c, t[a][j], s);
+        first = false;
+      }
       v[a][b] = s;
     }
 }
@@ -125,9 +143,14 @@ __device__ __forceinline__ void output_transform(const float (&mm)[M + 2][M + 2]
 #pragma unroll
     for (int b = 0; b < TD; ++b) {
       float s = 0.f;
+      bool first = true;
 #pragma unroll
-      for (int a = 0; a < TD; ++a)
-        if (Wino<M>::at(i, a) != 0.f) s = madd<EXACT>(Wino<M>::at(i, a), mm[a][b], s);
+      for (int a = 0; a < TD; ++a) {
+        const float c = Wino<M>::at(i, a);
+        if (c == 0.f) continue;
+        s = first ? first_term<EXACT>(c, mm[a][b]) : madd<EXACT>(c, mm[a][b], s);
+        first = false;
+      }
       t[i][b] = s;
     }
 #pragma unroll
@@ -135,9 +158,14 @@ __device__ __forceinline__ void output_transform(const float (&mm)[M + 2][M + 2]
 #pragma unroll
     for (int j = 0; j < M; ++j) {
       float s = 0.f;
+      bool first = true;
 #pragma unroll
-      for (int b = 0; b < TD; ++b)
-        if (Wino<M>::at(j, b) != 0.f) s = madd<EXACT>(Wino<M>::at(j, b), t[i][b], s);
+      for (int b = 0; b < TD; ++b) {
+        const float c = Wino<M>::at(j, b);
+        if (c == 0.f) continue;
+        s = first ? first_term<EXACT>(c, t[i][b]) : madd<EXACT>(c, t[i][b], s);
+        first = false;
+      }
       y[i][j] = s;
     }
 }

@@ -36,8 +36,15 @@ constexpr int kCout = 128;     // MMA M
 constexpr int kCc = 16;        // input channels per pipeline stage (one MMA K step)
 constexpr int kNF = 16;        // frequencies of F(2,3)
 constexpr int kFPerU = 2;      // frequencies per U stage
+#ifndef CWG_TC_NU
+#define CWG_TC_NU 3
+#endif
+#ifndef CWG_TC_MINB
+#define CWG_TC_MINB 2
+#endif
 constexpr int kNV = 2;         // V stages
-constexpr int kNU = 3;         // U stages
+constexpr int kNU = CWG_TC_NU; // U stages
+constexpr int kMinBlocks = CWG_TC_MINB;  // CTAs per SM the register budget targets
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr int kCoreBytes = 4096;               // one 128x16 bf16 operand block
@@ -155,6 +162,18 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {
   v[2] = __uint_as_float(r2);
   v[3] = __uint_as_float(r3);
 }
+// One lane of a converged warp (elect.sync).  Issuing tcgen05 instructions this
+// way, from warp-uniform control flow, keeps their operands in uniform
+// registers: a per-lane branch around them costs ~3x in MMA issue rate.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred px;\n\telect.sync _|px, %1;\n\t@px mov.s32 %0, 1;\n\t}"
+      : "+r"(pred)
+      : "r"(0xFFFFFFFFu));
+  return pred != 0;
+}
+
 // Named barrier 1: TMEM address handoff from warp 0 to the epilogue warps.
 constexpr int kBarTmem = 1;
 __device__ __forceinline__ void named_bar_arrive(int id, int count) {
@@ -194,11 +213,26 @@ __host__ __device__ constexpr uint32_t blk_off(int row, int k) {
   return (uint32_t)((row >> 3) * 256 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo_elem, float hi_elem) {
-  // element with the lower k index goes to the lower half
-  const uint32_t a = __bfloat16_as_ushort(__float2bfloat16_rn(lo_elem));
-  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(hi_elem));
-  return a | (b << 16);
+// Two fp32 values -> packed bf16x2 (first value in the low half), one cvt.
+__device__ __forceinline__ uint32_t pack_bf16(float first, float second) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(first, second);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// fp32 bit pattern rounded to the nearest bfloat16 (ties to even), returned as
+// an fp32 bit pattern with the low 16 bits clear.  Integer arithmetic only, so
+// the split below leaves the conversion pipe to the `lo` halves.
+__device__ __forceinline__ uint32_t round_bf16_bits(uint32_t u) {
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+}
+
+// hi = bf16(v), lo = bf16(v - hi) for a pair of values; each result packs the
+// pair (first value in the low half).
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t &hi, uint32_t &lo) {
+  const uint32_t ha = round_bf16_bits(__float_as_uint(a));
+  const uint32_t hb = round_bf16_bits(__float_as_uint(b));
+  hi = __byte_perm(ha, hb, 0x7632);
+  lo = pack_bf16(a - __uint_as_float(ha), b - __uint_as_float(hb));
 }
 
 // ---- weight transform into UMMA blocks ------------------------------------------
@@ -261,7 +295,7 @@ __global__ void wt_transform_tc(const float *__restrict__ src, uint8_t *__restri
 
 // ---- the fused kernel -------------------------------------------------------------
 template <bool X3, typename Tio>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, kMinBlocks)
     wino_fused_tc(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                   const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H, int W,
                   int tiles_y, int tiles_x, long long total_tiles, int relu) {
@@ -275,7 +309,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::kAbortSlot);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kTmemSlot);
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0);  // warp-uniform
+  const int lane = threadIdx.x & 31;
   const int C16 = (C + kCc - 1) / kCc;
   const int kblk = blockIdx.y;
   const long long tile0 = (long long)blockIdx.x * kTiles;
@@ -309,44 +344,55 @@ __global__ void __launch_bounds__(kThreads, 2)
     named_bar_arrive(kBarTmem, 32 + 128);  // hands the address to the epilogue warps
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (lane == 0) {
+    {
+      // The whole warp walks the pipeline; one elected lane issues.
       constexpr uint32_t idesc = instr_desc(kCout, kTiles);
+      constexpr uint32_t kLo = (uint32_t)(kNF * kVBytes) >> 4;  // V hi -> V lo
+      const uint64_t a0 = smem_desc(sbase + L::kUOff, 128, 256);
+      const uint64_t b0 = smem_desc(sbase + L::kVOff, 128, 256);
       bool ok = true;
       int ui = 0;
-      for (int cs = 0; cs < C16 && ok; ++cs) {
+      for (int cs = 0; cs < C16; ++cs) {
         const int vs = cs % kNV;
-        if (!(ok = mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort))) break;
+        ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort));
+        if (!ok) break;
         tc_fence_after();
-        const uint32_t vbase = sbase + L::kVOff + vs * L::kVStage;
+        const uint64_t bst = b0 + (uint64_t)((uint32_t)(vs * L::kVStage) >> 4);
+        const uint32_t acc0 = cs > 0 ? 1u : 0u;
+#pragma unroll
         for (int fp = 0; fp < kNF / kFPerU; ++fp, ++ui) {
           const int us = ui % kNU;
-          if (!(ok = mbar_wait(u_full + 8 * us, (ui / kNU) & 1, abort))) break;
+          ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, (ui / kNU) & 1, abort));
+          if (!ok) break;
           tc_fence_after();
-          const uint32_t ubase = sbase + L::kUOff + us * L::kUStage;
+          const uint64_t ast = a0 + (uint64_t)((uint32_t)(us * L::kUStage) >> 4);
 #pragma unroll
           for (int fi = 0; fi < kFPerU; ++fi) {
             const int f = fp * kFPerU + fi;
             const uint32_t d = tmem + (uint32_t)(f * kTiles);
-            const uint32_t a_hi = ubase + (fi * P) * kCoreBytes;
-            const uint32_t b_hi = vbase + f * kVBytes;
-            const uint64_t ah = smem_desc(a_hi, 128, 256), bh = smem_desc(b_hi, 128, 256);
-            mma_bf16(d, ah, bh, idesc, cs > 0 ? 1u : 0u);
+            const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * kCoreBytes) >> 4);
+            const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
+            if (elect_one()) mma_bf16(d, ah, bh, idesc, acc0);
             if (X3) {
-              const uint64_t al = smem_desc(a_hi + kCoreBytes, 128, 256);
-              const uint64_t bl = smem_desc(b_hi + kNF * kVBytes, 128, 256);
-              mma_bf16(d, ah, bl, idesc, 1u);
-              mma_bf16(d, al, bh, idesc, 1u);
+              if (elect_one()) mma_bf16(d, ah, bh + kLo, idesc, 1u);
+              if (elect_one()) mma_bf16(d, ah + (uint64_t)(kCoreBytes >> 4), bh, idesc, 1u);
             }
           }
-          tc_commit(u_empty + 8 * us);
+          __syncwarp();
+          if (elect_one()) tc_commit(u_empty + 8 * us);
+          __syncwarp();
         }
-        if (ok) tc_commit(v_empty + 8 * vs);
+        if (!ok) break;
+        if (elect_one()) tc_commit(v_empty + 8 * vs);
+        __syncwarp();
       }
       if (ok) {
-        tc_commit(acc_full);
+        if (elect_one()) tc_commit(acc_full);
+        __syncwarp();
       } else {
         // drain whatever was issued before giving up
-        tc_commit(drain);
+        if (elect_one()) tc_commit(drain);
+        __syncwarp();
         const unsigned long long t0 = globaltimer();
         while (!mbar_try(drain, 0) && globaltimer() - t0 < kTimeoutNs) {
         }
@@ -354,30 +400,34 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else if (warp == 1) {
     // ---------------- producer: U stages by bulk copy ----------------
-    if (lane == 0) {
-      const int nstages = C16 * (kNF / kFPerU);
-      const uint8_t *ublk = U + (size_t)kblk * C16 * kNF * P * kCoreBytes;
-      int issued = 0;
-      for (int i = 0; i < nstages; ++i) {
-        const int s = i % kNU;
-        if (!mbar_wait(u_empty + 8 * s, ((i / kNU) & 1) ^ 1, abort)) break;
+    const int nstages = C16 * (kNF / kFPerU);
+    const uint8_t *ublk = U + (size_t)kblk * C16 * kNF * P * kCoreBytes;
+    int issued = 0;
+    for (int i = 0; i < nstages; ++i) {
+      const int s = i % kNU;
+      if (!__all_sync(0xffffffffu, mbar_wait(u_empty + 8 * s, ((i / kNU) & 1) ^ 1, abort)))
+        break;
+      if (elect_one()) {
         mbar_expect_tx(u_full + 8 * s, L::kUStage);
         bulk_g2s(sbase + L::kUOff + s * L::kUStage, ublk + (size_t)i * L::kUStage, L::kUStage,
                  u_full + 8 * s);
-        issued = i + 1;
       }
-      // never leave the CTA with a copy still writing shared memory
-      for (int i = issued - kNU > 0 ? issued - kNU : 0; i < issued; ++i) {
-        const int s = i % kNU;
-        const unsigned long long t0 = globaltimer();
-        while (!mbar_try(u_full + 8 * s, (i / kNU) & 1) && globaltimer() - t0 < kTimeoutNs) {
-        }
+      __syncwarp();
+      issued = i + 1;
+    }
+    // never leave the CTA with a copy still writing shared memory
+    for (int i = issued - kNU > 0 ? issued - kNU : 0; i < issued; ++i) {
+      const int s = i % kNU;
+      const unsigned long long t0 = globaltimer();
+      while (!mbar_try(u_full + 8 * s, (i / kNU) & 1) && globaltimer() - t0 < kTimeoutNs) {
       }
     }
   } else {
     // ---------------- transform warps, then epilogue ----------------
     const int tw = warp - 2;            // 0..3
-    const int r = lane >> 2, g = lane & 3;
+    // lane -> (tile r of 8, channel group g of 4).  Each half-warp then stores
+    // one contiguous 128-byte K half of the operand block: no bank conflicts.
+    const int r = (lane >> 1) & 7, g = ((lane >> 4) << 1) | (lane & 1);
     const int t = tw * 8 + r;           // tile within the CTA
     const long long T = tile0 + t;
     const bool tile_ok = T < total_tiles;
@@ -429,21 +479,17 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int f = 0; f < kNF; ++f) {
         const int a = f >> 2, b = f & 3;
-        float e0 = v[0][a][b], e1 = v[1][a][b], e2 = v[2][a][b], e3 = v[3][a][b];
-        uint2 hi;
-        hi.x = pack_bf16(e0, e1);
-        hi.y = pack_bf16(e2, e3);
-        *reinterpret_cast<uint2 *>(vb + f * kVBytes + off) = hi;
+        const float e0 = v[0][a][b], e1 = v[1][a][b], e2 = v[2][a][b], e3 = v[3][a][b];
+        uint2 hi, lo;
         if (X3) {
-          const float h0 = __bfloat162float(__float2bfloat16_rn(e0));
-          const float h1 = __bfloat162float(__float2bfloat16_rn(e1));
-          const float h2 = __bfloat162float(__float2bfloat16_rn(e2));
-          const float h3 = __bfloat162float(__float2bfloat16_rn(e3));
-          uint2 lo;
-          lo.x = pack_bf16(e0 - h0, e1 - h1);
-          lo.y = pack_bf16(e2 - h2, e3 - h3);
+          split_pair(e0, e1, hi.x, lo.x);
+          split_pair(e2, e3, hi.y, lo.y);
           *reinterpret_cast<uint2 *>(vb + (kNF + f) * kVBytes + off) = lo;
+        } else {
+          hi.x = pack_bf16(e0, e1);
+          hi.y = pack_bf16(e2, e3);
         }
+        *reinterpret_cast<uint2 *>(vb + f * kVBytes + off) = hi;
       }
       fence_proxy_async();
       __syncwarp();
@@ -458,42 +504,65 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort));
     tc_fence_after();
     if (ok) {
+      // Lane = output channel after tcgen05.ld.  Each group of 8 tiles is
+      // transposed through a private shared-memory patch (row stride 33
+      // floats: conflict-free both ways) so that every warp store then writes
+      // two contiguous 64-byte row segments of one channel plane.  The operand
+      // stages are free: every MMA has completed.
       const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
-      const int k = kblk * kCout + quad * 32 + lane;
-      const float bk = (bias != nullptr && k < K) ? bias[k] : 0.f;
+      const int kq = kblk * kCout + quad * 32;
       const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+      float *patch = reinterpret_cast<float *>(smem) + (warp - 2) * (32 * 33);
+      const float bk = (bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
+      const long long per_img = (long long)tiles_y * tiles_x;
+      // this lane's output pixel in the read-back phase: tile j, pixel (pi, pj)
+      const int jt = lane >> 2, pi = (lane >> 1) & 1, pj = lane & 1;
 #pragma unroll 1
-      for (int gq = 0; gq < kTiles / 4; ++gq) {
-        float acc[kNF][4];
+      for (int gq = 0; gq < kTiles / 8; ++gq) {
+        float acc[kNF][8];
 #pragma unroll
-        for (int f = 0; f < kNF; ++f) tmem_ld4(trow + (uint32_t)(f * kTiles + gq * 4), acc[f]);
+        for (int f = 0; f < kNF; ++f) {
+          float lo4[4], hi4[4];
+          tmem_ld4(trow + (uint32_t)(f * kTiles + gq * 8), lo4);
+          tmem_ld4(trow + (uint32_t)(f * kTiles + gq * 8 + 4), hi4);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            acc[f][e] = lo4[e];
+            acc[f][4 + e] = hi4[e];
+          }
+        }
         tmem_wait_ld();
-        if (k >= K) continue;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const long long TT = tile0 + gq * 4 + j;
-          if (TT >= total_tiles) break;
-          const long long per_img = (long long)tiles_y * tiles_x;
-          const int nn = (int)(TT / per_img);
-          const int rem = (int)(TT - (long long)nn * per_img);
-          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
+        for (int j = 0; j < 8; ++j) {
           float mm[4][4], o[2][2];
 #pragma unroll
           for (int f = 0; f < kNF; ++f) mm[f >> 2][f & 3] = acc[f][j];
           output_transform<2>(mm, o);
-          Tio *yk = y + ((size_t)nn * K + k) * plane;
 #pragma unroll
           for (int i = 0; i < 2; ++i)
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
-              const int oy = 2 * yy + i, ox = 2 * xx + jj;
-              if (oy < H && ox < W) {
-                float val = o[i][jj] + bk;
-                if (relu) val = val < 0.f ? 0.f : val;
-                yk[(size_t)oy * W + ox] = from_f32<Tio>(val);
-              }
+              float val = o[i][jj] + bk;
+              if (relu) val = val < 0.f ? 0.f : val;
+              patch[lane * 33 + j * 4 + i * 2 + jj] = val;
             }
         }
+        __syncwarp();
+        const long long TT = tile0 + gq * 8 + jt;
+        if (TT < total_tiles) {
+          const int nn = (int)(TT / per_img);
+          const int rem = (int)(TT - (long long)nn * per_img);
+          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
+          const int oy = 2 * yy + pi, ox = 2 * xx + pj;
+          if (oy < H && ox < W) {
+            Tio *dst = y + ((size_t)nn * K + kq) * plane + (size_t)oy * W + ox;
+            const int kmax = K - kq < 32 ? K - kq : 32;
+#pragma unroll 4
+            for (int cc = 0; cc < kmax; ++cc)
+              dst[(size_t)cc * plane] = from_f32<Tio>(patch[cc * 33 + jt * 4 + pi * 2 + pj]);
+          }
+        }
+        __syncwarp();
       }
     }
   }

@@ -17,7 +17,7 @@ from dataclasses import dataclass
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libcwg.so")
+LIB_PATH = os.environ.get("CWG_LIB") or os.path.join(HERE, "lib", "libcwg.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "cwg.h")
 
 # status codes and flags (include/cwg.h)
