@@ -80,7 +80,7 @@ static int num_sms(void) {
  * weight layout chosen at transform time matches the conv call) ----------- */
 static int tc_available(int x3) {
   cwgk_tc_cfg cfg;
-  return cwgk_tc_get_cfg(x3, &cfg) == 0;
+  return cwgk_tc_get_cfg(x3, 0, &cfg) == 0;
 }
 
 /* Tensor cores only where the per-frequency GEMM is a real contraction: both
@@ -181,7 +181,8 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
                    4.0 * c_out;
   if (path == CWG_PATH_TC) {
     cwgk_tc_cfg t;
-    cwgk_tc_get_cfg(layout_of(path, flags) == CWGK_LAYOUT_TC_X3, &t);
+    cwgk_tc_get_cfg(layout_of(path, flags) == CWGK_LAYOUT_TC_X3, (flags & CWG_TC_FULL16) != 0,
+                    &t);
     out->tiles_per_cta = t.tiles;
     out->cout_per_cta = t.kb;
     out->cin_chunk = t.cc;
@@ -250,7 +251,8 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   const int bf16 = (flags & CWG_BF16) ? 1 : 0;
   if (path == CWG_PATH_TC) {
     const int x3 = layout_of(path, flags) == CWGK_LAYOUT_TC_X3;
-    return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, x3, bf16, relu, stream);
+    return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, x3, (flags & CWG_TC_FULL16) != 0,
+                        bf16, relu, stream);
   }
   cwgk_ffma_cfg cfg;
   const int idx = pick_ffma(n, c_out, h, w, mm, &cfg);

@@ -42,7 +42,7 @@ typedef struct cwgk_tc_cfg {
 
 int cwgk_ffma_num_cfgs(void);
 int cwgk_ffma_get_cfg(int idx, cwgk_ffma_cfg *out);
-int cwgk_tc_get_cfg(int x3, cwgk_tc_cfg *out);
+int cwgk_tc_get_cfg(int x3, int full16, cwgk_tc_cfg *out);
 
 /* g (or U_ref when from_ref) -> U in `layout`.  Device pointers. */
 int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m, int layout,
@@ -56,9 +56,11 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
 int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
                    int c_in, int c_out, int h, int w, int bf16, int relu, void *stream);
 
-/* tcgen05 fused convolution (F(2,3); c_in % 16 == 0, c_out % 128 == 0). */
+/* tcgen05 fused convolution, F(2,3) (C_in padded to 16, C_out to 128 by the
+ * weight layout).  full16: plain 16-accumulator scheme instead of the
+ * half-folded one. */
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
-                 int c_out, int h, int w, int x3, int bf16, int relu, void *stream);
+                 int c_out, int h, int w, int x3, int full16, int bf16, int relu, void *stream);
 
 /* Per-tile kernel on device buffers (reference layouts). */
 int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,

@@ -31,30 +31,45 @@
 namespace cwg {
 namespace tc {
 
-constexpr int kTiles = 32;     // MMA N
 constexpr int kCout = 128;     // MMA M
 constexpr int kCc = 16;        // input channels per pipeline stage (one MMA K step)
 constexpr int kNF = 16;        // frequencies of F(2,3)
 constexpr int kFPerU = 2;      // frequencies per U stage
-#ifndef CWG_TC_NU
-#define CWG_TC_NU 3
-#endif
-#ifndef CWG_TC_MINB
-#define CWG_TC_MINB 2
-#endif
 constexpr int kNV = 2;         // V stages
-constexpr int kNU = CWG_TC_NU; // U stages
-constexpr int kMinBlocks = CWG_TC_MINB;  // CTAs per SM the register budget targets
-constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr int kCoreBytes = 4096;               // one 128x16 bf16 operand block
-constexpr int kVBytes = kTiles * kCc * 2;      // one 32x16 bf16 operand block (1 KiB)
 constexpr unsigned long long kTimeoutNs = 2000000000ull;  // 2 s per wait
 
-template <bool X3>
+// Two accumulation schemes share the kernel:
+//   HALF  ("half-folded", the default): the row pass of the output transform,
+//         Z[i][b] = sum_a At[i][a] M[a][b], runs inside the GEMM (the MMA's
+//         negate-A bit supplies At's -1 entries), so 8 accumulators of 64 tiles
+//         fill TMEM.  1.5x the MACs of plain Winograd, but every U byte serves 64
+//         tiles instead of 32 and N=64 MMAs run ~1.7x closer to peak than N=32.
+//   full: the 16 frequency accumulators M[a][b] of 32 tiles (plain Winograd).
+template <bool HALF>
+struct Geo {
+  static constexpr int kTiles = HALF ? 64 : 32;         // MMA N
+  static constexpr int kAcc = HALF ? 8 : 16;            // TMEM accumulators
+  static constexpr int kXWarps = HALF ? 8 : 4;          // transform + epilogue warps
+  static constexpr int kThreads = (2 + kXWarps) * 32;
+  static constexpr int kMinBlocks = HALF ? 1 : 2;       // CTAs per SM
+  static constexpr int kNU = HALF ? 5 : 3;              // U stages
+  static constexpr int kVBytes = kTiles * kCc * 2;      // one N x 16 bf16 operand block
+  static_assert(kAcc * kTiles == kTmemCols, "accumulators fill TMEM");
+};
+
+// At of F(2,3) (src/fused_winograd_kernel.py:25-28), for the half-folded GEMM.
+__host__ __device__ constexpr int at23(int i, int a) {
+  return i == 0 ? (a == 3 ? 0 : 1) : (a == 0 ? 0 : (a == 1 ? 1 : -1));
+}
+
+template <bool X3, bool HALF>
 struct Layout {
+  using G = Geo<HALF>;
+  static constexpr int kNU = G::kNU;
   static constexpr int kParts = X3 ? 2 : 1;                       // hi (+ lo)
-  static constexpr int kVStage = kParts * kNF * kVBytes;          // 16 or 32 KiB
+  static constexpr int kVStage = kParts * kNF * G::kVBytes;       // up to 64 KiB
   static constexpr int kUStage = kFPerU * kParts * kCoreBytes;    // 8 or 16 KiB
   static constexpr int kVOff = 0;
   static constexpr int kUOff = kVOff + kNV * kVStage;
@@ -294,13 +309,16 @@ __global__ void wt_transform_tc(const float *__restrict__ src, uint8_t *__restri
 }
 
 // ---- the fused kernel -------------------------------------------------------------
-template <bool X3, typename Tio>
-__global__ void __launch_bounds__(kThreads, kMinBlocks)
+template <bool X3, bool HALF, typename Tio>
+__global__ void __launch_bounds__(Geo<HALF>::kThreads, Geo<HALF>::kMinBlocks)
     wino_fused_tc(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                   const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H, int W,
                   int tiles_y, int tiles_x, long long total_tiles, int relu) {
-  using L = Layout<X3>;
+  using L = Layout<X3, HALF>;
+  using G = Geo<HALF>;
   constexpr int P = L::kParts;
+  constexpr int kTiles = G::kTiles, kNU = G::kNU, kVBytes = G::kVBytes;
+  constexpr int kEpiThreads = 32 * G::kXWarps;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const uint32_t v_full = sbase + L::kBarOff, v_empty = v_full + 8 * kNV;
@@ -317,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNV; ++i) {
-      mbar_init(v_full + 8 * i, 4);
+      mbar_init(v_full + 8 * i, G::kXWarps);
       mbar_init(v_empty + 8 * i, 1);
     }
     for (int i = 0; i < kNU; ++i) {
@@ -341,15 +359,18 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     tc_fence_before();
     __syncwarp();
-    named_bar_arrive(kBarTmem, 32 + 128);  // hands the address to the epilogue warps
+    named_bar_arrive(kBarTmem, 32 + kEpiThreads);  // hands the address to the epilogue warps
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     {
       // The whole warp walks the pipeline; one elected lane issues.
       constexpr uint32_t idesc = instr_desc(kCout, kTiles);
+      constexpr uint32_t idesc_neg = idesc | (1u << 13);  // negate A
       constexpr uint32_t kLo = (uint32_t)(kNF * kVBytes) >> 4;  // V hi -> V lo
       const uint64_t a0 = smem_desc(sbase + L::kUOff, 128, 256);
-      const uint64_t b0 = smem_desc(sbase + L::kVOff, 128, 256);
+      // V blocks are K-half-major: the two 8-channel halves kTiles*16 bytes
+      // apart, 8-tile row groups 128 bytes apart.
+      const uint64_t b0 = smem_desc(sbase + L::kVOff, (uint32_t)(kTiles * 16), 128);
       bool ok = true;
       int ui = 0;
       for (int cs = 0; cs < C16; ++cs) {
@@ -369,13 +390,24 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 #pragma unroll
           for (int fi = 0; fi < kFPerU; ++fi) {
             const int f = fp * kFPerU + fi;
-            const uint32_t d = tmem + (uint32_t)(f * kTiles);
             const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * kCoreBytes) >> 4);
             const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
-            if (elect_one()) mma_bf16(d, ah, bh, idesc, acc0);
-            if (X3) {
-              if (elect_one()) mma_bf16(d, ah, bh + kLo, idesc, 1u);
-              if (elect_one()) mma_bf16(d, ah + (uint64_t)(kCoreBytes >> 4), bh, idesc, 1u);
+#pragma unroll
+            for (int i = 0; i < (HALF ? 2 : 1); ++i) {
+              const int a = f >> 2, b = f & 3;
+              const int sgn = HALF ? at23(i, a) : 1;
+              if (sgn == 0) continue;
+              // accumulator: Z[i][b] (half-folded) or M[a][b]
+              const int q = HALF ? i * 4 + b : f;
+              const uint32_t d = tmem + (uint32_t)(q * kTiles);
+              const uint32_t id = sgn < 0 ? idesc_neg : idesc;
+              // the first term of Z[i][b] is a = i (At[0][0] = At[1][1] = 1)
+              const uint32_t first = HALF ? (a == i ? acc0 : 1u) : acc0;
+              if (elect_one()) mma_bf16(d, ah, bh, id, first);
+              if (X3) {
+                if (elect_one()) mma_bf16(d, ah, bh + kLo, id, 1u);
+                if (elect_one()) mma_bf16(d, ah + (uint64_t)(kCoreBytes >> 4), bh, id, 1u);
+              }
             }
           }
           __syncwarp();
@@ -424,11 +456,15 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     }
   } else {
     // ---------------- transform warps, then epilogue ----------------
-    const int tw = warp - 2;            // 0..3
-    // lane -> (tile r of 8, channel group g of 4).  Each half-warp then stores
-    // one contiguous 128-byte K half of the operand block: no bank conflicts.
-    const int r = (lane >> 1) & 7, g = ((lane >> 4) << 1) | (lane & 1);
-    const int t = tw * 8 + r;           // tile within the CTA
+    const int tw = warp - 2;            // 0 .. kXWarps-1
+    // warp -> (16-tile block, 8-channel half kh); lane -> (tile, 4-channel
+    // group).  A warp load then reads 16 consecutive tiles of 2 channel planes
+    // (2 x 128 contiguous bytes) and a warp store fills 256 contiguous bytes of
+    // the K-half-major V block: coalesced and free of bank conflicts.
+    constexpr int kTileBlocks = kTiles / 16;
+    const int kh = tw / kTileBlocks;
+    const int g = 2 * kh + (lane & 1);  // channels 4g .. 4g+3 of the stage
+    const int t = (tw % kTileBlocks) * 16 + (lane >> 1);  // tile within the CTA
     const long long T = tile0 + t;
     const bool tile_ok = T < total_tiles;
     int n = 0, ty = 0, tx = 0;
@@ -472,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
       ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
       if (!ok) break;
       uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
-      const uint32_t off = blk_off(t, g * 4);
+      const uint32_t off = (uint32_t)(kh * (kTiles * 16) + t * 16 + (lane & 1) * 8);
       float v[4][4][4];
 #pragma unroll
       for (int q = 0; q < 4; ++q) input_transform<2>(d[q], v[q]);
@@ -498,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     }
 
     // ---------------- epilogue ----------------
-    named_bar_sync(kBarTmem, 32 + 128);
+    named_bar_sync(kBarTmem, 32 + kEpiThreads);
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort));
@@ -510,34 +546,48 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
       // two contiguous 64-byte row segments of one channel plane.  The operand
       // stages are free: every MMA has completed.
       const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
+      const int col0 = (tw / 4) * 32;  // this warp's 32 tile columns
       const int kq = kblk * kCout + quad * 32;
       const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-      float *patch = reinterpret_cast<float *>(smem) + (warp - 2) * (32 * 33);
+      float *patch = reinterpret_cast<float *>(smem) + tw * (32 * 33);
       const float bk = (bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
       const long long per_img = (long long)tiles_y * tiles_x;
       // this lane's output pixel in the read-back phase: tile j, pixel (pi, pj)
       const int jt = lane >> 2, pi = (lane >> 1) & 1, pj = lane & 1;
 #pragma unroll 1
-      for (int gq = 0; gq < kTiles / 8; ++gq) {
-        float acc[kNF][8];
+      for (int gq = 0; gq < (kTiles / G::kXWarps * 4) / 8; ++gq) {
+        const int cbase = col0 + gq * 8;
+        float acc[G::kAcc][8];
 #pragma unroll
-        for (int f = 0; f < kNF; ++f) {
+        for (int q = 0; q < G::kAcc; ++q) {
           float lo4[4], hi4[4];
-          tmem_ld4(trow + (uint32_t)(f * kTiles + gq * 8), lo4);
-          tmem_ld4(trow + (uint32_t)(f * kTiles + gq * 8 + 4), hi4);
+          tmem_ld4(trow + (uint32_t)(q * kTiles + cbase), lo4);
+          tmem_ld4(trow + (uint32_t)(q * kTiles + cbase + 4), hi4);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            acc[f][e] = lo4[e];
-            acc[f][4 + e] = hi4[e];
+            acc[q][e] = lo4[e];
+            acc[q][4 + e] = hi4[e];
           }
         }
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          float mm[4][4], o[2][2];
+          float o[2][2];
+          if (HALF) {
+            // Y[i][j'] = sum_b Z[i][b] At[j'][b]
 #pragma unroll
-          for (int f = 0; f < kNF; ++f) mm[f >> 2][f & 3] = acc[f][j];
-          output_transform<2>(mm, o);
+            for (int i = 0; i < 2; ++i) {
+              const float z0 = acc[i * 4 + 0][j], z1 = acc[i * 4 + 1][j];
+              const float z2 = acc[i * 4 + 2][j], z3 = acc[i * 4 + 3][j];
+              o[i][0] = (z0 + z1) + z2;
+              o[i][1] = (z1 - z2) - z3;
+            }
+          } else {
+            float mm[4][4];
+#pragma unroll
+            for (int f = 0; f < kNF; ++f) mm[f >> 2][f & 3] = acc[f][j];
+            output_transform<2>(mm, o);
+          }
 #pragma unroll
           for (int i = 0; i < 2; ++i)
 #pragma unroll
@@ -548,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
             }
         }
         __syncwarp();
-        const long long TT = tile0 + gq * 8 + jt;
+        const long long TT = tile0 + cbase + jt;
         if (TT < total_tiles) {
           const int nn = (int)(TT / per_img);
           const int rem = (int)(TT - (long long)nn * per_img);
@@ -577,19 +627,20 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   }
 }
 
-template <bool X3, typename Tio>
+template <bool X3, bool HALF, typename Tio>
 static cudaError_t launch(const void *x, const void *U, const float *bias, void *y, int n, int c,
                           int k, int h, int w, int relu, cudaStream_t s) {
+  constexpr int kTiles = Geo<HALF>::kTiles;
   const int tiles_y = (h + 1) / 2, tiles_x = (w + 1) / 2;
   const long long total = (long long)n * tiles_y * tiles_x;
   const long long gx = (total + kTiles - 1) / kTiles;
   const int gy = (k + kCout - 1) / kCout;
   if (gx > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidValue;
-  auto fn = wino_fused_tc<X3, Tio>;
+  auto fn = wino_fused_tc<X3, HALF, Tio>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Layout<X3>::kSmem);
+                                       Layout<X3, HALF>::kSmem);
   if (e != cudaSuccess) return e;
-  fn<<<dim3((unsigned)gx, (unsigned)gy), kThreads, Layout<X3>::kSmem, s>>>(
+  fn<<<dim3((unsigned)gx, (unsigned)gy), Geo<HALF>::kThreads, Layout<X3, HALF>::kSmem, s>>>(
       (const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y, tiles_x, total,
       relu);
   return cudaGetLastError();
@@ -602,14 +653,15 @@ using namespace cwg;
 
 extern "C" {
 
-int cwgk_tc_get_cfg(int x3, cwgk_tc_cfg *out) {
+int cwgk_tc_get_cfg(int x3, int full16, cwgk_tc_cfg *out) {
   if (!out) return -1;
   out->m = 2;
-  out->tiles = tc::kTiles;
+  out->tiles = full16 ? tc::Geo<false>::kTiles : tc::Geo<true>::kTiles;
   out->kb = tc::kCout;
   out->cc = tc::kCc;
-  out->threads = tc::kThreads;
-  out->smem = x3 ? tc::Layout<true>::kSmem : tc::Layout<false>::kSmem;
+  out->threads = full16 ? tc::Geo<false>::kThreads : tc::Geo<true>::kThreads;
+  out->smem = full16 ? (x3 ? tc::Layout<true, false>::kSmem : tc::Layout<false, false>::kSmem)
+                     : (x3 ? tc::Layout<true, true>::kSmem : tc::Layout<false, true>::kSmem);
   out->tmem_cols = tc::kTmemCols;
   return 0;
 }
@@ -639,16 +691,17 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
 }
 
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
-                 int c_out, int h, int w, int x3, int bf16, int relu, void *stream) {
+                 int c_out, int h, int w, int x3, int full16, int bf16, int relu, void *stream) {
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
-  if (x3) {
-    e = bf16 ? tc::launch<true, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s)
-             : tc::launch<true, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s);
-  } else {
-    e = bf16 ? tc::launch<false, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s)
-             : tc::launch<false, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s);
-  }
+#define CWG_TC_LAUNCH(X3_, HALF_)                                                              \
+  (bf16 ? tc::launch<X3_, HALF_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s) \
+        : tc::launch<X3_, HALF_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
+  if (x3)
+    e = full16 ? CWG_TC_LAUNCH(true, false) : CWG_TC_LAUNCH(true, true);
+  else
+    e = full16 ? CWG_TC_LAUNCH(false, false) : CWG_TC_LAUNCH(false, true);
+#undef CWG_TC_LAUNCH
   cwgk_count_launch();
   if (e != cudaSuccess) {
     cwgk_set_cuda_error((int)e);

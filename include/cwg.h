@@ -52,6 +52,8 @@ extern "C" {
 #define CWG_FORCE_FFMA 0x10u /* ablation: always take the CUDA-core (FFMA) kernel */
 #define CWG_FORCE_TC 0x20u   /* ablation: always take the tcgen05 kernel (EUNSUPPORTED if it cannot) */
 #define CWG_TC_SINGLE 0x40u  /* ablation: fp32 I/O with ONE bf16 product per MAC (below fp32 parity) */
+#define CWG_TC_FULL16 0x80u  /* ablation: tensor-core kernel with all 16 frequency accumulators
+                                (32-tile blocks) instead of the half-folded 8 (64-tile blocks) */
 
 /* Kernel paths reported by cwg_select. */
 #define CWG_PATH_FFMA 1 /* warp register-blocked FFMA fused kernel */
