@@ -122,6 +122,23 @@ int cwg_conv3x3_fused_host(const void *x_host, const void *U, const float *bias,
                            void *workspace, size_t workspace_bytes, int n, int c_in, int c_out,
                            int h, int w, int m, unsigned flags, void *stream);
 
+/* For callers that cannot allocate device memory (a framework's allocator
+ * owns the device heap, a plug-in host hands over only host buffers and a
+ * stream, or a real-time path may not allocate after start-up): the same call
+ * as cwg_conv3x3_fused_host, but staging x and y in a fixed device array of
+ * CWG_STATIC_WORKSPACE_BYTES that the library holds on every GPU that loads
+ * it, so the call allocates nothing.  No counterpart in the reference.
+ * Limits: cwg_host_workspace_bytes(n, c_in, c_out, h, w, flags) must not
+ * exceed CWG_STATIC_WORKSPACE_BYTES (CWG_EUNSUPPORTED otherwise).  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress);
+ * make that first call before any stream capture.  All calls share the one
+ * array: calls whose work overlaps on the GPU (different streams or threads
+ * without ordering) race on it. */
+#define CWG_STATIC_WORKSPACE_BYTES (32u << 20)
+int cwg_conv3x3_fused_host_static(const void *x_host, const void *U, const float *bias,
+                                  void *y_host, int n, int c_in, int c_out, int h, int w, int m,
+                                  unsigned flags, void *stream);
+
 /* ---- selector, diagnostics ----------------------------------------------- */
 
 /* Chooses m (when m == 0), the kernel path and its blocking for a layer on the
