@@ -31,6 +31,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.join(ROOT, "cache-aware-wino-implementation_b200")
 sys.path.insert(0, PKG)
 
+import ranks  # noqa: E402
 import workloads  # noqa: E402
 
 METRIC = ("µs/layer and effective conv TFLOP/s (2·N·K·C·H·W·9) "
@@ -124,11 +125,13 @@ def cpu_time_layer(layer, n_images: int, reps: int = 3):
     td = layer.m + 2
     U = oracle.weight_transform(g, td)
     use_ref = layer.m == 2 and oracle.ref_available()
+    # every core this process may run on (torchrun exports OMP_NUM_THREADS=1)
+    nthreads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
     def run(xx):
         if use_ref:
-            return oracle.ref_conv_layer_f23(xx, U, bias, layer.relu)
-        return oracle.conv_layer(xx, U, bias, td, layer.relu)
+            return oracle.ref_conv_layer_f23(xx, U, bias, layer.relu, nthreads)
+        return oracle.conv_layer(xx, U, bias, td, layer.relu, nthreads)
 
     run(x[:1])  # warm-up
     times = []
@@ -213,9 +216,8 @@ def main() -> None:
     if args.warmup < 3:
         args.warmup = 3
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rk = ranks.from_env()
+    rank, world, local = rk.rank, rk.world, rk.local
     layer = workloads.config_layers(args.config)[args.layer]
 
     if args.impl == "reference":
@@ -223,16 +225,12 @@ def main() -> None:
         return
 
     import torch
-    import torch.distributed as dist
 
     import cwg
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    ranks.init(rk, "nccl", device=dev)
 
     flags = (cwg.RELU if layer.relu else 0) | (cwg.BF16 if layer.bf16 else 0) | args.flags
     n, c, k, h, w, m = layer.n, layer.c_in, layer.c_out, layer.h, layer.w, layer.m
@@ -242,7 +240,8 @@ def main() -> None:
 
     # inputs: this rank's shard of the global batch, resident in HBM
     g, bias = workloads.make_weights(layer)
-    x_host = workloads.make_input(layer, n, first_image=rank * n)
+    first, _ = ranks.shard(n * world, rk)  # weak scaling: n images per rank
+    x_host = workloads.make_input(layer, n, first_image=first)
     x0 = torch.from_numpy(x_host).to(dev).to(dt)
     U = torch.empty(cwg.weight_bytes(c, k, m, flags), dtype=torch.uint8, device=dev)
     cwg.weight_transform(torch.from_numpy(g).to(dev), U, c, k, m, flags)
@@ -262,8 +261,7 @@ def main() -> None:
     cwg.device_status(stream)
 
     def barrier():
-        if world > 1:
-            dist.barrier()
+        ranks.barrier(rk)
         torch.cuda.synchronize(dev)
 
     # ---- timed region: K steps, events on the launching stream ----
@@ -279,11 +277,7 @@ def main() -> None:
     launches = cwg.launch_count() - launches0
     cwg.device_status(stream)
     t_ms = ev0.elapsed_time(ev1) / args.steps
-    t_max = t_ms
-    if world > 1:
-        tt = torch.tensor([t_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_max = float(tt.item())
+    t_max = ranks.max_over_ranks(t_ms, rk, dev)
 
     # ---- end to end through the host-buffer entry point ----
     xh = torch.from_numpy(x_host).to(dt).pin_memory() if layer.bf16 else \
@@ -306,20 +300,10 @@ def main() -> None:
         e2e_step()
     e1.record(stream)
     barrier()
-    te_ms = e0.elapsed_time(e1) / e2e_steps
-    if world > 1:
-        tt = torch.tensor([te_ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        te_ms = float(tt.item())
+    te_ms = ranks.max_over_ranks(e0.elapsed_time(e1) / e2e_steps, rk, dev)
 
     # ---- verification checksum of every rank's output (outside timing) ----
-    csum = torch.tensor([float(ys[0].double().sum().item())], dtype=torch.float64, device=dev)
-    if world > 1:
-        allc = [torch.zeros_like(csum) for _ in range(world)]
-        dist.all_gather(allc, csum)
-        checksums = [float(t.item()) for t in allc]
-    else:
-        checksums = [float(csum.item())]
+    checksums = ranks.gather_floats(float(ys[0].double().sum().item()), rk, dev)
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -371,9 +355,7 @@ def main() -> None:
             line["cpu_baseline"] = cpu_baseline(layer)
         print(json.dumps(line), flush=True)
 
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    ranks.finish(rk)
 
 
 if __name__ == "__main__":
