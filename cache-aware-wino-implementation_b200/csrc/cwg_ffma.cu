@@ -86,13 +86,19 @@ __global__ void wt_transform_ffma(const float *__restrict__ src, float *__restri
 // ============================================================================
 // Fused FFMA kernel
 // ============================================================================
-// CTA = TY x TX output tiles of one image x KB output channels.  Per step of CC
-// input channels: the (TY*M+2) x (TX*M+2) halo is staged in shared memory
-// (zero outside the image = pad 1), each (channel, tile) is transformed to V,
-// and every warp runs the GEMM of FPW frequencies, each lane holding a TR x KR
-// register block (tiles x channels).  The epilogue regroups the frequency
-// accumulators through shared memory, applies At M A, bias and ReLU, and
-// stores NCHW.
+// CTA = TY x TX output tiles of one image x KB output channels, looping over
+// the input channels in steps of CC.  Per step:
+//   * U[f][c0:c0+CC][k0:k0+KB] arrives by 16-byte cp.async into one of two
+//     buffers while the previous step computes (double buffering);
+//   * the (TY*M+2) x (TX*M+2) input halo of the step (zero outside the image =
+//     pad 1) was loaded into registers during the previous step and is now
+//     written to shared memory;
+//   * every thread transforms a slice of frequency rows of one (channel, tile)
+//     patch (Bt d B), so the whole CTA shares the transform;
+//   * each warp runs the GEMM of FPW frequencies, every lane holding a TR x KR
+//     register block (tiles x output channels).
+// The epilogue regroups the frequency accumulators through shared memory and
+// applies At M A, bias and ReLU, storing NCHW.
 template <int M, int TY, int TX, int KB, int CC, int FPW>
 struct FG {
   static constexpr int TD = M + 2, NF = TD * TD, T = TY * TX;
@@ -100,12 +106,19 @@ struct FG {
   static constexpr int KR = 4, KG = KB / KR, TG = 32 / KG, TR = T / TG;
   static constexpr int NW = NF / FPW, NT = NW * 32;
   static constexpr int XS = CC * HR * WR, VS = NF * CC * T, US = NF * CC * KB;
-  static constexpr int MAIN = XS + VS + US;
+  static constexpr int XPT = (XS + NT - 1) / NT;          // halo elements per thread
+  static constexpr int U4 = US / 4, U4PT = (U4 + NT - 1) / NT;  // 16-byte U chunks per thread
+  static constexpr int PAIRS = CC * T;                     // (channel, tile) patches per step
+  static constexpr int PARTS = NT / PAIRS;                 // threads per patch
+  static constexpr int ROWS = TD / PARTS;                  // frequency rows per thread
+  static constexpr int MAIN = XS + VS + 2 * US;
   static constexpr int EPI = NF * KG * (T + 1);
   static constexpr int SMEM = 4 * (MAIN > EPI ? MAIN : EPI);
   static_assert(NF % FPW == 0, "frequencies per warp must divide td^2");
   static_assert(KB % KR == 0 && 32 % KG == 0 && T % TG == 0, "lane grid must tile 32");
   static_assert(TR == 2 || TR % 4 == 0, "tile register block must vectorise");
+  static_assert(NT % PAIRS == 0 && TD % PARTS == 0, "transform slices must tile the CTA");
+  static_assert(KB % 4 == 0, "U rows copy in 16-byte chunks");
 };
 
 template <int N>
@@ -126,6 +139,69 @@ __device__ __forceinline__ void lds_vec(const float *p, float (&v)[N]) {
   }
 }
 
+// 16-byte global -> shared async copy; src_bytes < 16 zero-fills the rest.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, int src_bytes) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Row A of V = Bt d B: (Bt d)[A][:] then times B, coefficients as immediates.
+template <int M, int A>
+__device__ __forceinline__ void v_row(const float (&d)[M + 2][M + 2], float (&out)[M + 2]) {
+  constexpr int TD = M + 2;
+  float trow[TD];
+#pragma unroll
+  for (int j = 0; j < TD; ++j) {
+    float sacc = 0.f;
+    bool first = true;
+#pragma unroll
+    for (int i = 0; i < TD; ++i) {
+      const float cf = Wino<M>::bt(A, i);
+      if (cf == 0.f) continue;
+      sacc = first ? first_term<false>(cf, d[i][j]) : fmaf(cf, d[i][j], sacc);
+      first = false;
+    }
+    trow[j] = sacc;
+  }
+#pragma unroll
+  for (int b = 0; b < TD; ++b) {
+    float sacc = 0.f;
+    bool first = true;
+#pragma unroll
+    for (int j = 0; j < TD; ++j) {
+      const float cf = Wino<M>::bt(b, j);
+      if (cf == 0.f) continue;
+      sacc = first ? first_term<false>(cf, trow[j]) : fmaf(cf, trow[j], sacc);
+      first = false;
+    }
+    out[b] = sacc;
+  }
+}
+
+template <int M>
+__device__ __forceinline__ void v_row_dispatch(int a, const float (&d)[M + 2][M + 2],
+                                               float (&out)[M + 2]) {
+  switch (a) {
+    case 0: v_row<M, 0>(d, out); break;
+    case 1: v_row<M, 1>(d, out); break;
+    case 2: v_row<M, 2>(d, out); break;
+    case 3: v_row<M, 3>(d, out); break;
+    default:
+      if constexpr (M + 2 > 4) {
+        if (a == 4) v_row<M, 4>(d, out);
+        else v_row<M, 5>(d, out);
+      }
+  }
+}
+
 template <int M, int TY, int TX, int KB, int CC, int FPW, typename Tio>
 __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
     wino_fused_ffma(const Tio *__restrict__ x, const float *__restrict__ U,
@@ -136,7 +212,7 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
   extern __shared__ __align__(16) float smem[];
   float *xs = smem;
   float *vs = xs + G::XS;
-  float *us = vs + G::VS;
+  float *us0 = vs + G::VS;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tg = lane / KG, kg = lane % KG;
@@ -147,6 +223,52 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
   const int iy0 = ty0 * M - 1, ix0 = tx0 * M - 1;
   const size_t plane = (size_t)H * W;
   const Tio *xn = x + (size_t)n * C * plane;
+  const int steps = (C + CC - 1) / CC;
+  const bool u_vec = (K & 3) == 0;  // every U row starts on a 16-byte boundary
+
+  // ---- U step s -> us buffer (s & 1), 16-byte chunks (scalar if K % 4 != 0)
+  auto issue_u = [&](int st) {
+    float *dst = us0 + (st & 1) * G::US;
+    const int c0 = st * CC;
+#pragma unroll
+    for (int j = 0; j < G::U4PT; ++j) {
+      const int q = tid + j * NT;
+      if (q < G::U4) {
+        const int row = q / (KB / 4), k4 = (q - row * (KB / 4)) * 4;  // row = f * CC + c
+        const int f = row / CC, c = row - f * CC;
+        const int cg = c0 + c, kk = k0 + k4;
+        const float *src = U + ((size_t)f * C + (cg < C ? cg : 0)) * K + (kk < K ? kk : 0);
+        float *d = dst + row * KB + k4;
+        if (u_vec) {
+          const int bytes = (cg < C && kk < K) ? 16 : 0;
+          cp_async16(d, src, bytes);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            d[e] = (cg < C && kk + e < K) ? U[((size_t)f * C + cg) * K + kk + e] : 0.f;
+        }
+      }
+    }
+    cp_async_commit();
+  };
+  // ---- input halo of step s -> registers (stored to xs at the start of step s)
+  float xr[G::XPT];
+  auto load_x = [&](int st) {
+    const int c0 = st * CC;
+#pragma unroll
+    for (int j = 0; j < G::XPT; ++j) {
+      const int i = tid + j * NT;
+      float v = 0.f;
+      if (i < G::XS) {
+        const int c = i / (G::HR * G::WR), rem = i - c * (G::HR * G::WR);
+        const int r = rem / G::WR, s2 = rem - r * G::WR;
+        const int iy = iy0 + r, ix = ix0 + s2;
+        if (c0 + c < C && iy >= 0 && iy < H && ix >= 0 && ix < W)
+          v = to_f32(xn[(size_t)(c0 + c) * plane + (size_t)iy * W + ix]);
+      }
+      xr[j] = v;
+    }
+  };
 
   float acc[FPW][TR][KR];
 #pragma unroll
@@ -156,42 +278,48 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
 #pragma unroll
       for (int c = 0; c < KR; ++c) acc[a][b][c] = 0.f;
 
-  for (int c0 = 0; c0 < C; c0 += CC) {
-    // stage the input halo (zero outside the image and past C)
-    for (int i = tid; i < G::XS; i += NT) {
-      const int c = i / (G::HR * G::WR), rem = i - c * (G::HR * G::WR);
-      const int r = rem / G::WR, s = rem - r * G::WR;
-      const int iy = iy0 + r, ix = ix0 + s;
-      float v = 0.f;
-      if (c0 + c < C && iy >= 0 && iy < H && ix >= 0 && ix < W)
-        v = to_f32(xn[(size_t)(c0 + c) * plane + (size_t)iy * W + ix]);
-      xs[i] = v;
+  // this thread's transform slice: one (channel, tile) patch and ROWS
+  // frequency rows; the slice (part) is uniform across a warp.
+  const int part = warp % G::PARTS, tp = (warp / G::PARTS) * 32 + lane;
+  const int tc = tp / T, tt = tp - tc * T, tyl = tt / TX, txl = tt - tyl * TX;
+
+  issue_u(0);
+  load_x(0);
+  for (int st = 0; st < steps; ++st) {
+    // stage this step's halo, prefetch the next step
+#pragma unroll
+    for (int j = 0; j < G::XPT; ++j) {
+      const int i = tid + j * NT;
+      if (i < G::XS) xs[i] = xr[j];
     }
-    // stage U[f][c0:c0+CC][k0:k0+KB]
-    for (int i = tid; i < G::US; i += NT) {
-      const int k = i % KB, fc = i / KB, c = fc % CC, f = fc / CC;
-      float v = 0.f;
-      if (c0 + c < C && k0 + k < K) v = U[((size_t)f * C + c0 + c) * K + k0 + k];
-      us[i] = v;
+    if (st + 1 < steps) {
+      issue_u(st + 1);
+      load_x(st + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
-    // input transform: one (channel, tile) per thread
-    for (int p = tid; p < CC * T; p += NT) {
-      const int c = p / T, t = p - c * T, tyl = t / TX, txl = t - tyl * TX;
-      const float *src = xs + c * G::HR * G::WR + (tyl * M) * G::WR + txl * M;
-      float d[TD][TD], v[TD][TD];
+    // transform: rows [part*ROWS, part*ROWS+ROWS) of V for patch (tc, tt)
+    {
+      const float *src = xs + tc * G::HR * G::WR + (tyl * M) * G::WR + txl * M;
+      float d[TD][TD];
 #pragma unroll
       for (int r = 0; r < TD; ++r)
 #pragma unroll
-        for (int s = 0; s < TD; ++s) d[r][s] = src[r * G::WR + s];
-      input_transform<M>(d, v);
+        for (int c2 = 0; c2 < TD; ++c2) d[r][c2] = src[r * G::WR + c2];
 #pragma unroll
-      for (int a = 0; a < TD; ++a)
+      for (int ra = 0; ra < G::ROWS; ++ra) {
+        const int a = part * G::ROWS + ra;
+        float vrow[TD];
+        v_row_dispatch<M>(a, d, vrow);
 #pragma unroll
-        for (int b = 0; b < TD; ++b) vs[((a * TD + b) * CC + c) * T + t] = v[a][b];
+        for (int b2 = 0; b2 < TD; ++b2) vs[((a * TD + b2) * CC + tc) * T + tt] = vrow[b2];
+      }
     }
     __syncthreads();
     // per-frequency GEMM on the CUDA cores
+    const float *us = us0 + (st & 1) * G::US;
 #pragma unroll 2
     for (int c = 0; c < CC; ++c) {
 #pragma unroll
@@ -223,14 +351,15 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
     for (int p = tid; p < T * KG; p += NT) {
       const int t = p % T, kgp = p / T;
       const int k = k0 + kgp * KR + q;
-      const int tyl = t / TX, txl = t - tyl * TX;
-      const int ty = ty0 + tyl, tx = tx0 + txl;
+      const int tyl2 = t / TX, txl2 = t - tyl2 * TX;
+      const int ty = ty0 + tyl2, tx = tx0 + txl2;
       if (k < K && ty < tiles_y && tx < tiles_x) {
         float mm[TD][TD], yy[M][M];
 #pragma unroll
         for (int a = 0; a < TD; ++a)
 #pragma unroll
-          for (int b = 0; b < TD; ++b) mm[a][b] = ms[((a * TD + b) * KG + kgp) * (T + 1) + t];
+          for (int b2 = 0; b2 < TD; ++b2)
+            mm[a][b2] = ms[((a * TD + b2) * KG + kgp) * (T + 1) + t];
         output_transform<M>(mm, yy);
         const float bb = bias ? bias[k] : 0.f;
         Tio *yk = y + ((size_t)n * K + k) * plane;
@@ -336,8 +465,8 @@ struct FfmaEntry {
 static const FfmaEntry kFfma[] = {
     CWG_FFMA_ENTRY(2, 4, 4, 16, 8, 1), CWG_FFMA_ENTRY(2, 4, 4, 32, 8, 1),
     CWG_FFMA_ENTRY(2, 4, 4, 64, 8, 1), CWG_FFMA_ENTRY(2, 8, 8, 32, 8, 1),
-    CWG_FFMA_ENTRY(4, 4, 4, 16, 8, 2), CWG_FFMA_ENTRY(4, 4, 4, 32, 8, 2),
-    CWG_FFMA_ENTRY(4, 4, 4, 64, 8, 2),
+    CWG_FFMA_ENTRY(4, 4, 4, 16, 8, 3), CWG_FFMA_ENTRY(4, 4, 4, 32, 8, 3),
+    CWG_FFMA_ENTRY(4, 4, 4, 64, 8, 3),
 };
 constexpr int kNumFfma = sizeof(kFfma) / sizeof(kFfma[0]);
 
