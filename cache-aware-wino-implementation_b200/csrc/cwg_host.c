@@ -260,47 +260,7 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   return cwgk_conv_ffma(idx, x, U, bias, y, n, c_in, c_out, h, w, bf16, relu, stream);
 }
 
-size_t cwg_host_workspace_bytes(int n, int c_in, int c_out, int h, int w, unsigned flags) {
-  if (n < 0 || c_in <= 0 || c_out <= 0 || h <= 0 || w <= 0) return 0;
-  const size_t esz = (flags & CWG_BF16) ? 2 : 4;
-  const size_t xb = ((size_t)n * c_in * h * w * esz + 255) / 256 * 256;
-  const size_t yb = ((size_t)n * c_out * h * w * esz + 255) / 256 * 256;
-  return xb + yb;
-}
-
-int cwg_conv3x3_fused_host(const void *x_host, const void *U, const float *bias, void *y_host,
-                           void *workspace, size_t workspace_bytes, int n, int c_in, int c_out,
-                           int h, int w, int m, unsigned flags, void *stream) {
-  const size_t need = cwg_host_workspace_bytes(n, c_in, c_out, h, w, flags);
-  if (need == 0 || !x_host || !y_host || !workspace || workspace_bytes < need ||
-      ((uintptr_t)workspace & 255))
-    return CWG_EINVAL;
-  const size_t esz = (flags & CWG_BF16) ? 2 : 4;
-  const size_t xbytes = (size_t)n * c_in * h * w * esz;
-  const size_t ybytes = (size_t)n * c_out * h * w * esz;
-  char *xd = (char *)workspace;
-  char *yd = xd + (xbytes + 255) / 256 * 256;
-  cudaStream_t s = (cudaStream_t)stream;
-  cudaError_t e = cudaMemcpyAsync(xd, x_host, xbytes, cudaMemcpyHostToDevice, s);
-  if (e != cudaSuccess) return cuda_fail(e);
-  int rc = cwg_conv3x3_fused(xd, U, bias, yd, n, c_in, c_out, h, w, m, flags, stream);
-  if (rc) return rc;
-  e = cudaMemcpyAsync(y_host, yd, ybytes, cudaMemcpyDeviceToHost, s);
-  if (e != cudaSuccess) return cuda_fail(e);
-  e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return cuda_fail(e);
-  return CWG_OK;
-}
-
-int cwg_device_status(void *stream) {
-  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
-  if (e != cudaSuccess) return cuda_fail(e);
-  unsigned st = 0;
-  if (cwgk_read_clear_status(&st)) return CWG_ECUDA;
-  return st ? CWG_ETIMEOUT : CWG_OK;
-}
-
-/* ---- per-tile entry points (host buffers) -------------------------------- */
+/* ---- per-thread context: staging for the per-tile calls, copy streams ---- */
 
 /* Per-thread staging: a stream and one device buffer that grows on demand.
  * Freed by the thread-exit destructor; the main thread's copy lives until
@@ -310,6 +270,10 @@ typedef struct tile_ctx {
   cudaStream_t stream;
   void *buf;
   size_t cap;
+  /* copy streams and events of the pipelined host-buffer layer call */
+  cudaStream_t s_in, s_out;
+  cudaEvent_t ev_start, ev_in, ev_comp, ev_done;
+  int pipe_ready;
 } tile_ctx;
 
 static pthread_key_t g_ctx_key;
@@ -321,6 +285,14 @@ static void ctx_free(void *p) {
   if (!c) return;
   if (c->buf) cudaFree(c->buf);
   if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->pipe_ready) {
+    cudaStreamDestroy(c->s_in);
+    cudaStreamDestroy(c->s_out);
+    cudaEventDestroy(c->ev_start);
+    cudaEventDestroy(c->ev_in);
+    cudaEventDestroy(c->ev_comp);
+    cudaEventDestroy(c->ev_done);
+  }
   free(c);
 }
 
@@ -348,7 +320,7 @@ static int ctx_get(size_t need, tile_ctx **out) {
     }
     pthread_setspecific(g_ctx_key, c);
   }
-  if (c->cap < need) {
+  if (need > 0 && c->cap < need) {
     if (c->buf) cudaFree(c->buf);
     c->buf = NULL;
     c->cap = 0;
@@ -361,6 +333,113 @@ static int ctx_get(size_t need, tile_ctx **out) {
   }
   *out = c;
   return CWG_OK;
+}
+
+size_t cwg_host_workspace_bytes(int n, int c_in, int c_out, int h, int w, unsigned flags) {
+  if (n < 0 || c_in <= 0 || c_out <= 0 || h <= 0 || w <= 0) return 0;
+  const size_t esz = (flags & CWG_BF16) ? 2 : 4;
+  const size_t xb = ((size_t)n * c_in * h * w * esz + 255) / 256 * 256;
+  const size_t yb = ((size_t)n * c_out * h * w * esz + 255) / 256 * 256;
+  return xb + yb;
+}
+
+/* One stream: copy x in, convolve, copy y out, synchronise.  Creates nothing
+ * and allocates nothing (the no-allocation entry point relies on that). */
+int cwgh_conv_host_serial(const void *x_host, const void *U, const float *bias, void *y_host,
+                          char *xd, char *yd, size_t xbytes, size_t ybytes, int n, int c_in,
+                          int c_out, int h, int w, int m, unsigned flags, void *stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaMemcpyAsync(xd, x_host, xbytes, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  int rc = cwg_conv3x3_fused(xd, U, bias, yd, n, c_in, c_out, h, w, m, flags, s);
+  if (rc) return rc;
+  e = cudaMemcpyAsync(y_host, yd, ybytes, cudaMemcpyDeviceToHost, s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  return CWG_OK;
+}
+
+static int pipe_ready(tile_ctx *c) {
+  if (c->pipe_ready) return CWG_OK;
+  cudaError_t e = cudaStreamCreateWithFlags(&c->s_in, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->s_out, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_start, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_in, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_comp, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_done, cudaEventDisableTiming);
+  if (e != cudaSuccess) return cuda_fail(e);
+  c->pipe_ready = 1;
+  return CWG_OK;
+}
+
+/* Large layers: the batch is cut into image chunks; chunk i's copy-in (copy
+ * stream), convolution (caller's stream) and copy-out (second copy stream)
+ * overlap with the neighbouring chunks, so the call costs about one
+ * direction of host<->device traffic instead of both plus the kernel. */
+#define HOST_PIPE_MIN_BYTES (8u << 20)
+#define HOST_PIPE_CHUNKS 16
+
+int cwg_conv3x3_fused_host(const void *x_host, const void *U, const float *bias, void *y_host,
+                           void *workspace, size_t workspace_bytes, int n, int c_in, int c_out,
+                           int h, int w, int m, unsigned flags, void *stream) {
+  const size_t need = cwg_host_workspace_bytes(n, c_in, c_out, h, w, flags);
+  if (need == 0 || !x_host || !y_host || !workspace || workspace_bytes < need ||
+      ((uintptr_t)workspace & 255))
+    return CWG_EINVAL;
+  const size_t esz = (flags & CWG_BF16) ? 2 : 4;
+  const size_t xbytes = (size_t)n * c_in * h * w * esz;
+  const size_t ybytes = (size_t)n * c_out * h * w * esz;
+  char *xd = (char *)workspace;
+  char *yd = xd + (xbytes + 255) / 256 * 256;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (n < 2 || xbytes + ybytes < HOST_PIPE_MIN_BYTES)
+    return cwgh_conv_host_serial(x_host, U, bias, y_host, xd, yd, xbytes, ybytes, n, c_in, c_out,
+                                 h, w, m, flags, s);
+  tile_ctx *c = NULL;
+  int rc = ctx_get(0, &c);
+  if (rc) return rc;
+  rc = pipe_ready(c);
+  if (rc) return rc;
+  const size_t xi = xbytes / (size_t)n, yi = ybytes / (size_t)n;  /* bytes per image */
+  const int chunks = n < HOST_PIPE_CHUNKS ? n : HOST_PIPE_CHUNKS;
+  /* everything already queued on the caller's stream comes first */
+  cudaError_t e = cudaEventRecord(c->ev_start, s);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_in, c->ev_start, 0);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_out, c->ev_start, 0);
+  if (e != cudaSuccess) return cuda_fail(e);
+  int done = 0;
+  for (int i = 0; i < chunks; ++i) {
+    const int cnt = (n - done) / (chunks - i);
+    const size_t xo = (size_t)done * xi, yo = (size_t)done * yi;
+    e = cudaMemcpyAsync(xd + xo, (const char *)x_host + xo, (size_t)cnt * xi,
+                        cudaMemcpyHostToDevice, c->s_in);
+    if (e == cudaSuccess) e = cudaEventRecord(c->ev_in, c->s_in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, c->ev_in, 0);
+    if (e != cudaSuccess) return cuda_fail(e);
+    rc = cwg_conv3x3_fused(xd + xo, U, bias, yd + yo, cnt, c_in, c_out, h, w, m, flags, stream);
+    if (rc) return rc;
+    e = cudaEventRecord(c->ev_comp, s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_out, c->ev_comp, 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync((char *)y_host + yo, yd + yo, (size_t)cnt * yi,
+                          cudaMemcpyDeviceToHost, c->s_out);
+    if (e != cudaSuccess) return cuda_fail(e);
+    done += cnt;
+  }
+  e = cudaEventRecord(c->ev_done, c->s_out);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s, c->ev_done, 0);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e);
+  return CWG_OK;
+}
+
+int cwg_device_status(void *stream) {
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e);
+  unsigned st = 0;
+  if (cwgk_read_clear_status(&st)) return CWG_ECUDA;
+  return st ? CWG_ETIMEOUT : CWG_OK;
 }
 
 static size_t al256(size_t b) { return (b + 255) / 256 * 256; }

@@ -66,6 +66,12 @@ int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n
 int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,
                int td, void *stream);
 
+/* Host-buffer layer call on one stream (copy in, convolve, copy out, sync),
+ * staging in xd/yd; creates and allocates nothing. */
+int cwgh_conv_host_serial(const void *x_host, const void *U, const float *bias, void *y_host,
+                          char *xd, char *yd, size_t xbytes, size_t ybytes, int n, int c_in,
+                          int c_out, int h, int w, int m, unsigned flags, void *stream);
+
 /* Reads and clears the device status word (after the caller synchronised). */
 int cwgk_read_clear_status(unsigned *status);
 

@@ -62,7 +62,13 @@ extern "C" int cwg_conv3x3_fused_host_static(const void *x_host, const void *U,
   const int rc = static_workspace(&ws);
   if (rc != CWG_OK) return rc;
   // x and y are overwritten in full by the copy-in and by the kernel, so the
-  // previous call's contents never leak into this one.
-  return cwg_conv3x3_fused_host(x_host, U, bias, y_host, ws, need, n, c_in, c_out, h, w, m,
-                                flags, stream);
+  // previous call's contents never leak into this one.  One stream, nothing
+  // created or allocated.
+  const size_t esz = (flags & CWG_BF16) ? 2 : 4;
+  const size_t xbytes = (size_t)n * c_in * h * w * esz;
+  const size_t ybytes = (size_t)n * c_out * h * w * esz;
+  char *xd = static_cast<char *>(ws);
+  char *yd = xd + (xbytes + 255) / 256 * 256;
+  return cwgh_conv_host_serial(x_host, U, bias, y_host, xd, yd, xbytes, ybytes, n, c_in, c_out,
+                               h, w, m, flags, stream);
 }
