@@ -51,7 +51,8 @@ template <bool HALF>
 struct Geo {
   static constexpr int kTiles = HALF ? 64 : 32;         // MMA N
   static constexpr int kAcc = HALF ? 8 : 16;            // TMEM accumulators
-  static constexpr int kXWarps = HALF ? 8 : 4;          // transform + epilogue warps
+  static constexpr int kXWarps = HALF ? 16 : 4;         // transform + epilogue warps
+  static constexpr int kCpt = kTiles * 16 / (32 * kXWarps);  // channels per transform thread
   static constexpr int kThreads = (2 + kXWarps) * 32;
   static constexpr int kMinBlocks = HALF ? 1 : 2;       // CTAs per SM
   static constexpr int kNU = HALF ? 5 : 3;              // U stages
@@ -457,13 +458,14 @@ __global__ void __launch_bounds__(Geo<HALF>::kThreads, Geo<HALF>::kMinBlocks)
   } else {
     // ---------------- transform warps, then epilogue ----------------
     const int tw = warp - 2;            // 0 .. kXWarps-1
-    // warp -> (16-tile block, 8-channel half kh); lane -> (tile, 4-channel
-    // group).  A warp load then reads 16 consecutive tiles of 2 channel planes
-    // (2 x 128 contiguous bytes) and a warp store fills 256 contiguous bytes of
-    // the K-half-major V block: coalesced and free of bank conflicts.
-    constexpr int kTileBlocks = kTiles / 16;
-    const int kh = tw / kTileBlocks;
-    const int g = 2 * kh + (lane & 1);  // channels 4g .. 4g+3 of the stage
+    // warp -> (16-tile block, group of 2*CPT channels); lane -> (tile, CPT
+    // channels).  A warp load then reads 16 consecutive tiles of 2 channel
+    // planes (2 x 64-128 contiguous bytes) and a warp store fills one
+    // contiguous run of the K-half-major V block.
+    constexpr int kTileBlocks = kTiles / 16, CPT = G::kCpt;
+    const int cgrp = tw / kTileBlocks;
+    const int cbase = cgrp * (2 * CPT) + (lane & 1) * CPT;  // first channel of the stage
+    const int kh = cbase >> 3;                               // K half of the MMA step
     const int t = (tw % kTileBlocks) * 16 + (lane >> 1);  // tile within the CTA
     const long long T = tile0 + t;
     const bool tile_ok = T < total_tiles;
@@ -485,11 +487,11 @@ __global__ void __launch_bounds__(Geo<HALF>::kThreads, Geo<HALF>::kMinBlocks)
       rv[i] = tile_ok && (y0 + i) >= 0 && (y0 + i) < H;
       cv[i] = (x0 + i) >= 0 && (x0 + i) < W;
     }
-    float d[4][4][4];  // [channel of 4][row][col]
+    float d[CPT][4][4];  // [channel][row][col]
     auto load_stage = [&](int cs) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int c = cs * kCc + g * 4 + q;
+      for (int q = 0; q < CPT; ++q) {
+        const int c = cs * kCc + cbase + q;
         const bool cok = c < C;
         const Tio *xc = xn + (size_t)c * plane;
 #pragma unroll
@@ -508,24 +510,36 @@ __global__ void __launch_bounds__(Geo<HALF>::kThreads, Geo<HALF>::kMinBlocks)
       ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
       if (!ok) break;
       uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
-      const uint32_t off = (uint32_t)(kh * (kTiles * 16) + t * 16 + (lane & 1) * 8);
-      float v[4][4][4];
+      const uint32_t off = (uint32_t)(kh * (kTiles * 16) + t * 16 + (cbase & 7) * 2);
+      float v[CPT][4][4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) input_transform<2>(d[q], v[q]);
+      for (int q = 0; q < CPT; ++q) input_transform<2>(d[q], v[q]);
 #pragma unroll
       for (int f = 0; f < kNF; ++f) {
         const int a = f >> 2, b = f & 3;
-        const float e0 = v[0][a][b], e1 = v[1][a][b], e2 = v[2][a][b], e3 = v[3][a][b];
-        uint2 hi, lo;
-        if (X3) {
-          split_pair(e0, e1, hi.x, lo.x);
-          split_pair(e2, e3, hi.y, lo.y);
-          *reinterpret_cast<uint2 *>(vb + (kNF + f) * kVBytes + off) = lo;
+        if constexpr (CPT == 4) {
+          const float e0 = v[0][a][b], e1 = v[1][a][b], e2 = v[2][a][b], e3 = v[3][a][b];
+          uint2 hi, lo;
+          if (X3) {
+            split_pair(e0, e1, hi.x, lo.x);
+            split_pair(e2, e3, hi.y, lo.y);
+            *reinterpret_cast<uint2 *>(vb + (kNF + f) * kVBytes + off) = lo;
+          } else {
+            hi.x = pack_bf16(e0, e1);
+            hi.y = pack_bf16(e2, e3);
+          }
+          *reinterpret_cast<uint2 *>(vb + f * kVBytes + off) = hi;
         } else {
-          hi.x = pack_bf16(e0, e1);
-          hi.y = pack_bf16(e2, e3);
+          const float e0 = v[0][a][b], e1 = v[1][a][b];
+          uint32_t hi, lo;
+          if (X3) {
+            split_pair(e0, e1, hi, lo);
+            *reinterpret_cast<uint32_t *>(vb + (kNF + f) * kVBytes + off) = lo;
+          } else {
+            hi = pack_bf16(e0, e1);
+          }
+          *reinterpret_cast<uint32_t *>(vb + f * kVBytes + off) = hi;
         }
-        *reinterpret_cast<uint2 *>(vb + f * kVBytes + off) = hi;
       }
       fence_proxy_async();
       __syncwarp();
@@ -546,7 +560,8 @@ __global__ void __launch_bounds__(Geo<HALF>::kThreads, Geo<HALF>::kMinBlocks)
       // two contiguous 64-byte row segments of one channel plane.  The operand
       // stages are free: every MMA has completed.
       const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
-      const int col0 = (tw / 4) * 32;  // this warp's 32 tile columns
+      constexpr int kCols = kTiles * 4 / G::kXWarps;  // tile columns per epilogue warp
+      const int col0 = (tw / 4) * kCols;
       const int kq = kblk * kCout + quad * 32;
       const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
       float *patch = reinterpret_cast<float *>(smem) + tw * (32 * 33);
@@ -555,7 +570,7 @@ __global__ void __launch_bounds__(Geo<HALF>::kThreads, Geo<HALF>::kMinBlocks)
       // this lane's output pixel in the read-back phase: tile j, pixel (pi, pj)
       const int jt = lane >> 2, pi = (lane >> 1) & 1, pj = lane & 1;
 #pragma unroll 1
-      for (int gq = 0; gq < (kTiles / G::kXWarps * 4) / 8; ++gq) {
+      for (int gq = 0; gq < kCols / 8; ++gq) {
         const int cbase = col0 + gq * 8;
         float acc[G::kAcc][8];
 #pragma unroll
