@@ -80,7 +80,15 @@ static int num_sms(void) {
  * weight layout chosen at transform time matches the conv call) ----------- */
 static int tc_available(int x3) {
   cwgk_tc_cfg cfg;
-  return cwgk_tc_get_cfg(x3, 0, &cfg) == 0;
+  return cwgk_tc_get_cfg(x3, CWGK_TC_PAIR, &cfg) == 0;
+}
+
+/* Tensor-core kernel variant: the 2-SM pair kernel unless a flag asks for one
+ * of the single-CTA kernels. */
+static int tc_variant(unsigned flags) {
+  if (flags & CWG_TC_FULL16) return CWGK_TC_FULL16;
+  if (flags & CWG_TC_NOPAIR) return CWGK_TC_HALF;
+  return CWGK_TC_PAIR;
 }
 
 /* Tensor cores only where the per-frequency GEMM is a real contraction: both
@@ -92,6 +100,7 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
   if (c_in <= 0 || c_out <= 0) return CWG_EINVAL;
   if (m != 0 && m != 2 && m != 4) return (m == 6) ? CWG_EUNSUPPORTED : CWG_EINVAL;
   if ((flags & CWG_FORCE_FFMA) && (flags & CWG_FORCE_TC)) return CWG_EINVAL;
+  if ((flags & CWG_TC_FULL16) && (flags & CWG_TC_NOPAIR)) return CWG_EINVAL;
   const int x3 = !(flags & (CWG_BF16 | CWG_TC_SINGLE));
   const int tc_ok = tc_available(x3) && tc_shape_ok(c_in, c_out) && (m == 0 || m == 2);
   if (flags & CWG_FORCE_TC) {
@@ -115,8 +124,11 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
 }
 
 static int layout_of(int path, unsigned flags) {
-  if (path == CWG_PATH_TC)
-    return (flags & (CWG_BF16 | CWG_TC_SINGLE)) ? CWGK_LAYOUT_TC_X1 : CWGK_LAYOUT_TC_X3;
+  if (path == CWG_PATH_TC) {
+    const int x1 = (flags & (CWG_BF16 | CWG_TC_SINGLE)) != 0;
+    if (tc_variant(flags) == CWGK_TC_PAIR) return x1 ? CWGK_LAYOUT_TC2_X1 : CWGK_LAYOUT_TC2_X3;
+    return x1 ? CWGK_LAYOUT_TC_X1 : CWGK_LAYOUT_TC_X3;
+  }
   /* The CUDA-core kernel keeps U in fp32 for bf16 layers too: rounding U to
    * bf16 loses ~4% through F(4,3)'s output transform (coefficients up to 8). */
   return CWGK_LAYOUT_FFMA_F32;
@@ -127,10 +139,14 @@ static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
   switch (layout) {
     case CWGK_LAYOUT_FFMA_F32: return nf * c_in * c_out * 4;
     case CWGK_LAYOUT_TC_X3:
-    case CWGK_LAYOUT_TC_X1: {
+    case CWGK_LAYOUT_TC_X1:
+    case CWGK_LAYOUT_TC2_X3:
+    case CWGK_LAYOUT_TC2_X1: {
       const size_t kp = ((size_t)c_out + 127) / 128 * 128;
       const size_t cp = ((size_t)c_in + 15) / 16 * 16;
-      return nf * kp * cp * (layout == CWGK_LAYOUT_TC_X3 ? 4 : 2);
+      const size_t parts = (layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3) ? 2 : 1;
+      const size_t sets = (layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1) ? 2 : 1;
+      return nf * kp * cp * 2 * parts * sets;
     }
     default: return 0;
   }
@@ -181,15 +197,16 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
                    4.0 * c_out;
   if (path == CWG_PATH_TC) {
     cwgk_tc_cfg t;
-    cwgk_tc_get_cfg(layout_of(path, flags) == CWGK_LAYOUT_TC_X3, (flags & CWG_TC_FULL16) != 0,
-                    &t);
+    const int lay = layout_of(path, flags);
+    cwgk_tc_get_cfg(lay == CWGK_LAYOUT_TC_X3 || lay == CWGK_LAYOUT_TC2_X3, tc_variant(flags), &t);
     out->tiles_per_cta = t.tiles;
     out->cout_per_cta = t.kb;
     out->cin_chunk = t.cc;
     out->threads = t.threads;
     out->smem_bytes = t.smem;
     out->tmem_cols = t.tmem_cols;
-    out->ctas = ((long long)n * th * tw + t.tiles - 1) / t.tiles * ((c_out + t.kb - 1) / t.kb);
+    out->ctas = ((long long)n * th * tw + t.tiles - 1) / t.tiles * ((c_out + t.kb - 1) / t.kb) *
+                t.ctas_per_tile_block;
   } else {
     cwgk_ffma_cfg c;
     if (pick_ffma(n, c_out, h, w, mm, &c) < 0) return CWG_EUNSUPPORTED;
@@ -250,9 +267,10 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   const int relu = (flags & CWG_RELU) ? 1 : 0;
   const int bf16 = (flags & CWG_BF16) ? 1 : 0;
   if (path == CWG_PATH_TC) {
-    const int x3 = layout_of(path, flags) == CWGK_LAYOUT_TC_X3;
-    return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, x3, (flags & CWG_TC_FULL16) != 0,
-                        bf16, relu, stream);
+    const int lay = layout_of(path, flags);
+    const int x3 = lay == CWGK_LAYOUT_TC_X3 || lay == CWGK_LAYOUT_TC2_X3;
+    return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, x3, tc_variant(flags), bf16, relu,
+                        stream);
   }
   cwgk_ffma_cfg cfg;
   const int idx = pick_ffma(n, c_out, h, w, mm, &cfg);

@@ -661,6 +661,494 @@ static cudaError_t launch(const void *x, const void *U, const float *bias, void 
   return cudaGetLastError();
 }
 
+// ==== 2-SM pair kernel (tcgen05.mma.cta_group::2) ====================================
+//
+// A CTA pair (a cluster of two, on the two SMs of one TPC) computes 128 output
+// channels x 128 tiles.  The half-folded accumulation is stacked along M:
+//   A (M = 256) = [At[0][a] U_ab ; At[1][a] U_ab]  -- rank r holds the 128 rows of
+//                 output-row parity i = r, pre-scaled by At (0 / +-1, exact);
+//   B (N = 128) = V_ab of the pair's 128 tiles     -- rank r holds tiles 64r..64r+63;
+//   D           = Z[i][b] = sum_a At[i][a] M[a][b] -- 4 accumulators x 128 tiles
+//                 per CTA: rank r's TMEM holds output row 2ty + r of every tile.
+// One MMA per (frequency, product) now serves both output rows and 128 tiles:
+// per SM the tensor core reads 6 KB of shared memory per 262K MACs instead of
+// 6 KB per 131K, and each CTA streams its weights once per 128 tiles.
+//
+// Rank 0 issues every MMA and commit for the pair.  Readiness of rank 1's
+// operands reaches rank 0 by remote mbarrier arrivals: rank 1's warp 0 (idle
+// otherwise) relays each of its completed V stages and landed weight stages.
+// Releases (operand stages, accumulators) are multicast commits that arrive on
+// both CTAs' barriers.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Arrival on a barrier of another CTA of the cluster.  Default (CTA-scope)
+// release: a cluster-scope release costs ~1.4K cycles per arrival, and what it
+// would order is already complete -- bulk copies by their own mbarrier, thread
+// writes to V by fence.proxy.async and the local barrier the relay observed.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+// completion of this thread's earlier MMAs -> one arrival on the barrier at
+// offset `bar` of every CTA in `mask`
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+__device__ __forceinline__ void mma_pair_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
+}
+
+// Pair weight layout: [K_pad/128][i = 2][C_pad/16][16 f][parts][4096 B block];
+// block (k, c) of frequency f = (a, b) holds At[i][a] * U_ab (sign flips and
+// zeros are exact in bf16).  Channels past C_out / C_in are zero.
+template <bool X3>
+__global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__restrict__ U,
+                                     int C, int K, int Cp, int Kp, int from_ref) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)Cp * Kp) return;
+  const int c = (int)(idx % Cp), k = (int)(idx / Cp);
+  float u[kNF];
+  if (k < K && c < C) {
+    if (from_ref) {
+#pragma unroll
+      for (int f = 0; f < kNF; ++f) u[f] = src[((long)k * C + c) * kNF + f];
+    } else {
+      // fp64 G g G^T, same operation order as the CPU oracle, rounded once
+      const double G[4][3] = {{1, 0, 0}, {.5, .5, .5}, {.5, -.5, .5}, {0, 0, 1}};
+      const float *g = src + ((long)k * C + c) * 9;
+      double t[4][3];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+          double s = 0.0;
+#pragma unroll
+          for (int i = 0; i < 3; ++i) s = __dadd_rn(s, __dmul_rn(G[a][i], (double)g[i * 3 + j]));
+          t[a][j] = s;
+        }
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          double s = 0.0;
+#pragma unroll
+          for (int j = 0; j < 3; ++j) s = __dadd_rn(s, __dmul_rn(t[a][j], G[b][j]));
+          u[a * 4 + b] = (float)s;
+        }
+    }
+  } else {
+#pragma unroll
+    for (int f = 0; f < kNF; ++f) u[f] = 0.f;
+  }
+  constexpr int parts = X3 ? 2 : 1;
+  const int C16 = Cp / kCc;
+  const uint32_t off = blk_off(k % kCout, c % kCc);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const long blk0 = ((long)(k / kCout) * 2 + i) * C16 + c / kCc;
+#pragma unroll
+    for (int f = 0; f < kNF; ++f) {
+      const int sgn = at23(i, f >> 2);
+      const __nv_bfloat16 hi = __float2bfloat16_rn(u[f]);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(u[f] - __bfloat162float(hi));
+      const __nv_bfloat16 z = __float2bfloat16_rn(0.f);
+      uint8_t *b = U + ((blk0 * kNF + f) * parts) * kCoreBytes;
+      *reinterpret_cast<__nv_bfloat16 *>(b + off) = sgn == 0 ? z : (sgn < 0 ? __hneg(hi) : hi);
+      if (X3)
+        *reinterpret_cast<__nv_bfloat16 *>(b + kCoreBytes + off) =
+            sgn == 0 ? z : (sgn < 0 ? __hneg(lo) : lo);
+    }
+  }
+}
+
+// Shared memory of one CTA of the pair: the operand rings of the half-folded
+// single-CTA kernel plus the relay barriers.
+template <bool X3>
+struct PairLayout {
+  using G = Geo<true>;
+  static constexpr int kNU = G::kNU;
+  static constexpr int kParts = X3 ? 2 : 1;
+  static constexpr int kVStage = kParts * kNF * G::kVBytes;     // 64 tiles
+  static constexpr int kUStage = kFPerU * kParts * kCoreBytes;
+  static constexpr int kVOff = 0;
+  static constexpr int kUOff = kVOff + kNV * kVStage;
+  static constexpr int kBarOff = kUOff + kNU * kUStage;
+  // v_full[kNV], v_empty[kNV], v_peer[kNV] (rank 0: rank 1's V stage written),
+  // u_full[kNU], u_empty[kNU], u_peer[kNU] (rank 0: rank 1's weights landed),
+  // acc_full, drain
+  static constexpr int kNumBars = 3 * kNV + 3 * kNU + 2;
+  static constexpr int kTmemSlot = kBarOff + 8 * kNumBars;
+  static constexpr int kAbortSlot = kTmemSlot + 4;
+  static constexpr int kSmem = kAbortSlot + 4;
+  static constexpr int kPatchFloats = 32 * 33;  // epilogue transpose, per warp
+  // the patches reuse the operand rings once every MMA has completed
+  static_assert(G::kXWarps * kPatchFloats * 4 <= kBarOff, "patches fit the operand rings");
+  static_assert(kSmem <= 227 * 1024, "fits the opt-in shared memory of one CTA");
+};
+
+constexpr int kPairTiles = 128;  // MMA N of the pair (64 tiles per CTA)
+
+template <bool X3, typename Tio>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads, 1)
+    wino_fused_tc_pair(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
+                       const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
+                       int W, int tiles_y, int tiles_x, long long total_tiles, int relu) {
+  using L = PairLayout<X3>;
+  using G = Geo<true>;
+  constexpr int P = L::kParts;
+  constexpr int kTiles = G::kTiles, kNU = L::kNU, kVBytes = G::kVBytes;
+  constexpr int kXW = G::kXWarps;
+  constexpr int kEpiThreads = 32 * kXW;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t v_full = sbase + L::kBarOff, v_empty = v_full + 8 * kNV;
+  const uint32_t v_peer = v_empty + 8 * kNV;
+  const uint32_t u_full = v_peer + 8 * kNV, u_empty = u_full + 8 * kNU;
+  const uint32_t u_peer = u_empty + 8 * kNU, acc_full = u_peer + 8 * kNU;
+  const uint32_t drain = acc_full + 8;
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + L::kAbortSlot);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kTmemSlot);
+
+  const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0);  // warp-uniform
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0: issues the MMAs; also the output-row parity
+  const int C16 = (C + kCc - 1) / kCc;
+  const int kblk = blockIdx.y;
+  const long long pair0 = (long long)(blockIdx.x >> 1) * kPairTiles;  // first tile of the pair
+  const long long tile0 = pair0 + (long long)rank * kTiles;          // this CTA's V columns
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNV; ++i) {
+      mbar_init(v_full + 8 * i, kXW);
+      mbar_init(v_empty + 8 * i, 1);
+      mbar_init(v_peer + 8 * i, 1);
+    }
+    for (int i = 0; i < kNU; ++i) {
+      mbar_init(u_full + 8 * i, 1);
+      mbar_init(u_empty + 8 * i, 1);
+      mbar_init(u_peer + 8 * i, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
+
+  if (warp == 0) {
+    // ---------------- TMEM (both CTAs) + MMA issue (rank 0) / relay (rank 1) ----------
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    tc_fence_before();
+    __syncwarp();
+    named_bar_arrive(kBarTmem, 32 + kEpiThreads);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int nstages = C16 * (kNF / kFPerU);
+    if (rank == 0) {
+      constexpr uint32_t idesc = instr_desc(2 * kCout, kPairTiles);
+      constexpr uint32_t kLo = (uint32_t)(kNF * kVBytes) >> 4;  // V hi -> V lo
+      const uint64_t a0 = smem_desc(sbase + L::kUOff, 128, 256);
+      const uint64_t b0 = smem_desc(sbase + L::kVOff, (uint32_t)(kTiles * 16), 128);
+      bool ok = true;
+      int ui = 0;
+      for (int cs = 0; cs < C16; ++cs) {
+        const int vs = cs % kNV;
+        ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort) &&
+                                         mbar_wait(v_peer + 8 * vs, (cs / kNV) & 1, abort));
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t bst = b0 + (uint64_t)((uint32_t)(vs * L::kVStage) >> 4);
+#pragma unroll
+        for (int fp = 0; fp < kNF / kFPerU; ++fp, ++ui) {
+          const int us = ui % kNU;
+          const uint32_t ph = (ui / kNU) & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, ph, abort) &&
+                                           mbar_wait(u_peer + 8 * us, ph, abort));
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t ast = a0 + (uint64_t)((uint32_t)(us * L::kUStage) >> 4);
+#pragma unroll
+          for (int fi = 0; fi < kFPerU; ++fi) {
+            const int f = fp * kFPerU + fi;
+            const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * kCoreBytes) >> 4);
+            const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
+            // accumulator Z[.][b]; its first term is a = 0 of the first stage
+            const uint32_t d = tmem + (uint32_t)((f & 3) * kPairTiles);
+            const uint32_t first = (cs > 0 || f >= 4) ? 1u : 0u;
+            if (elect_one()) mma_pair_bf16(d, ah, bh, idesc, first);
+            if (X3) {
+              if (elect_one()) mma_pair_bf16(d, ah, bh + kLo, idesc, 1u);
+              if (elect_one())
+                mma_pair_bf16(d, ah + (uint64_t)(kCoreBytes >> 4), bh, idesc, 1u);
+            }
+          }
+          __syncwarp();
+          if (elect_one()) tc_commit_pair(u_empty + 8 * us, 3);
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (elect_one()) tc_commit_pair(v_empty + 8 * vs, 3);
+        __syncwarp();
+      }
+      if (ok) {
+        if (elect_one()) tc_commit_pair(acc_full, 3);
+        __syncwarp();
+      } else {
+        // drain whatever was issued before giving up (the MMAs read both CTAs)
+        if (elect_one()) tc_commit_pair(drain, 1);
+        __syncwarp();
+        const unsigned long long t0 = globaltimer();
+        while (!mbar_try(drain, 0) && globaltimer() - t0 < kTimeoutNs) {
+        }
+      }
+    } else {
+      // relay, in the order rank 0 consumes them: each V stage written and each
+      // weight stage landed here -> one arrival on rank 0's barrier.
+      (void)nstages;
+      const uint32_t v_peer_r0 = mapa_shared(v_peer, 0), u_peer_r0 = mapa_shared(u_peer, 0);
+      int ui = 0;
+      bool ok = true;
+      for (int cs = 0; ok && cs < C16; ++cs) {
+        const int vs = cs % kNV;
+        ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort));
+        if (!ok) break;
+        if (elect_one()) mbar_arrive_cluster(v_peer_r0 + 8 * vs);
+        __syncwarp();
+        for (int fp = 0; fp < kNF / kFPerU; ++fp, ++ui) {
+          const int us = ui % kNU;
+          ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, (ui / kNU) & 1, abort));
+          if (!ok) break;
+          if (elect_one()) mbar_arrive_cluster(u_peer_r0 + 8 * us);
+          __syncwarp();
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- producer: this CTA's weight rows by bulk copy ----------------
+    const int nstages = C16 * (kNF / kFPerU);
+    const uint8_t *ublk = U + ((size_t)kblk * 2 + rank) * C16 * kNF * P * kCoreBytes;
+    int issued = 0;
+    for (int i = 0; i < nstages; ++i) {
+      const int s = i % kNU;
+      if (!__all_sync(0xffffffffu,
+                        mbar_wait(u_empty + 8 * s, ((i / kNU) & 1) ^ 1, abort)))
+        break;
+      if (elect_one()) {
+        mbar_expect_tx(u_full + 8 * s, L::kUStage);
+        bulk_g2s(sbase + L::kUOff + s * L::kUStage, ublk + (size_t)i * L::kUStage, L::kUStage,
+                 u_full + 8 * s);
+      }
+      __syncwarp();
+      issued = i + 1;
+    }
+    for (int i = issued - kNU > 0 ? issued - kNU : 0; i < issued; ++i) {
+      const int s = i % kNU;
+      const unsigned long long t0 = globaltimer();
+      while (!mbar_try(u_full + 8 * s, (i / kNU) & 1) && globaltimer() - t0 < kTimeoutNs) {
+      }
+    }
+  } else {
+    // ---------------- transform warps (this CTA's 64 tiles), then epilogue ----------
+    const int tw = warp - 2;
+    constexpr int kTileBlocks = kTiles / 16, CPT = G::kCpt;
+    static_assert(CPT == 2, "two channels per transform thread");
+    const int cgrp = tw / kTileBlocks;
+    const int cbase = cgrp * (2 * CPT) + (lane & 1) * CPT;
+    const int kh = cbase >> 3;
+    const int t = (tw % kTileBlocks) * 16 + (lane >> 1);
+    const long long T = tile0 + t;
+    const bool tile_ok = T < total_tiles;
+    int n = 0, ty = 0, tx = 0;
+    if (tile_ok) {
+      const long long per_img = (long long)tiles_y * tiles_x;
+      n = (int)(T / per_img);
+      const int rem = (int)(T - (long long)n * per_img);
+      ty = rem / tiles_x;
+      tx = rem - ty * tiles_x;
+    }
+    const int y0 = 2 * ty - 1, x0 = 2 * tx - 1;
+    const size_t plane = (size_t)H * W;
+    const Tio *xn = x + (size_t)n * C * plane;
+    bool rv[4], cv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      rv[i] = tile_ok && (y0 + i) >= 0 && (y0 + i) < H;
+      cv[i] = (x0 + i) >= 0 && (x0 + i) < W;
+    }
+    float d[CPT][4][4];
+    auto load_stage = [&](int cs) {
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) {
+        const int c = cs * kCc + cbase + q;
+        const bool cok = c < C;
+        const Tio *xc = xn + (size_t)c * plane;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            d[q][i][j] = (cok && rv[i] && cv[j])
+                             ? to_f32(xc[(size_t)(y0 + i) * W + (x0 + j)])
+                             : 0.f;
+      }
+    };
+    bool ok = true;
+    if (C16 > 0) load_stage(0);
+    for (int cs = 0; cs < C16; ++cs) {
+      const int vs = cs % kNV;
+      ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
+      if (!ok) break;
+      uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
+      const uint32_t off = (uint32_t)(kh * (kTiles * 16) + t * 16 + (cbase & 7) * 2);
+      float v[CPT][4][4];
+#pragma unroll
+      for (int q = 0; q < CPT; ++q) input_transform<2>(d[q], v[q]);
+#pragma unroll
+      for (int f = 0; f < kNF; ++f) {
+        const int a = f >> 2, b = f & 3;
+        const float e0 = v[0][a][b], e1 = v[1][a][b];
+        uint32_t hi, lo;
+        if (X3) {
+          split_pair(e0, e1, hi, lo);
+          *reinterpret_cast<uint32_t *>(vb + (kNF + f) * kVBytes + off) = lo;
+        } else {
+          hi = pack_bf16(e0, e1);
+        }
+        *reinterpret_cast<uint32_t *>(vb + f * kVBytes + off) = hi;
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(v_full + 8 * vs);
+      if (cs + 1 < C16) load_stage(cs + 1);
+    }
+
+    // ---------------- epilogue: output row 2ty + rank of the pair's 128 tiles ----------
+    named_bar_sync(kBarTmem, 32 + kEpiThreads);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort));
+    tc_fence_after();
+    if (ok) {
+      // Lane = output channel after tcgen05.ld.  Each group of 16 tiles (32
+      // output pixels of one row parity) goes through a private patch (row
+      // stride 33 floats) so that a warp store writes one contiguous 128-byte
+      // row segment of one channel plane.  Every MMA has completed and every
+      // weight copy landed: the operand rings of this CTA are free.
+      const int quad = warp & 3;
+      const int col0 = (tw >> 2) * (kPairTiles / 4);  // 32 tiles per warp
+      const int kq = kblk * kCout + quad * 32;
+      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+      float *patch = reinterpret_cast<float *>(smem + L::kVOff) + tw * L::kPatchFloats;
+      const float bk = (bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
+      const long long per_img = (long long)tiles_y * tiles_x;
+      const int kmax = K - kq < 32 ? K - kq : 32;
+#pragma unroll 1
+      for (int gq = 0; gq < 2; ++gq) {
+        const int cb = col0 + gq * 16;
+        float z[4][16];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) tmem_ld16(trow + (uint32_t)(b * kPairTiles + cb), z[b]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          // Y[i][0] = Z0 + Z1 + Z2, Y[i][1] = Z1 - Z2 - Z3
+          float o0 = (z[0][j] + z[1][j]) + z[2][j] + bk;
+          float o1 = (z[1][j] - z[2][j]) - z[3][j] + bk;
+          if (relu) {
+            o0 = o0 < 0.f ? 0.f : o0;
+            o1 = o1 < 0.f ? 0.f : o1;
+          }
+          patch[lane * 33 + 2 * j] = o0;
+          patch[lane * 33 + 2 * j + 1] = o1;
+        }
+        __syncwarp();
+        const long long TT = pair0 + cb + (lane >> 1);
+        if (TT < total_tiles && kmax > 0) {
+          const int nn = (int)(TT / per_img);
+          const int rem = (int)(TT - (long long)nn * per_img);
+          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
+          const int oy = 2 * yy + (int)rank, ox = 2 * xx + (lane & 1);
+          if (oy < H && ox < W) {
+            Tio *dst = y + ((size_t)nn * K + kq) * plane + (size_t)oy * W + ox;
+#pragma unroll 4
+            for (int cc = 0; cc < kmax; ++cc)
+              dst[(size_t)cc * plane] = from_f32<Tio>(patch[cc * 33 + lane]);
+          }
+        }
+        __syncwarp();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // rank 0's MMAs read both CTAs' shared memory and TMEM
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot),
+                 "r"(kTmemCols));
+  }
+}
+
+template <bool X3, typename Tio>
+static cudaError_t launch_pair(const void *x, const void *U, const float *bias, void *y, int n,
+                               int c, int k, int h, int w, int relu, cudaStream_t s) {
+  const int tiles_y = (h + 1) / 2, tiles_x = (w + 1) / 2;
+  const long long total = (long long)n * tiles_y * tiles_x;
+  const long long pairs = (total + kPairTiles - 1) / kPairTiles;
+  const int gy = (k + kCout - 1) / kCout;
+  if (2 * pairs > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidValue;
+  auto fn = wino_fused_tc_pair<X3, Tio>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       PairLayout<X3>::kSmem);
+  if (e != cudaSuccess) return e;
+  fn<<<dim3((unsigned)(2 * pairs), (unsigned)gy), Geo<true>::kThreads, PairLayout<X3>::kSmem,
+       s>>>((const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y, tiles_x,
+            total, relu);
+  return cudaGetLastError();
+}
+
 }  // namespace tc
 }  // namespace cwg
 
@@ -668,34 +1156,62 @@ using namespace cwg;
 
 extern "C" {
 
-int cwgk_tc_get_cfg(int x3, int full16, cwgk_tc_cfg *out) {
+int cwgk_tc_get_cfg(int x3, int variant, cwgk_tc_cfg *out) {
   if (!out) return -1;
   out->m = 2;
-  out->tiles = full16 ? tc::Geo<false>::kTiles : tc::Geo<true>::kTiles;
   out->kb = tc::kCout;
   out->cc = tc::kCc;
-  out->threads = full16 ? tc::Geo<false>::kThreads : tc::Geo<true>::kThreads;
-  out->smem = full16 ? (x3 ? tc::Layout<true, false>::kSmem : tc::Layout<false, false>::kSmem)
-                     : (x3 ? tc::Layout<true, true>::kSmem : tc::Layout<false, true>::kSmem);
   out->tmem_cols = tc::kTmemCols;
-  return 0;
+  switch (variant) {
+    case CWGK_TC_PAIR:
+      out->tiles = tc::kPairTiles;
+      out->threads = tc::Geo<true>::kThreads;
+      out->smem = x3 ? tc::PairLayout<true>::kSmem : tc::PairLayout<false>::kSmem;
+      out->ctas_per_tile_block = 2;
+      return 0;
+    case CWGK_TC_HALF:
+      out->tiles = tc::Geo<true>::kTiles;
+      out->threads = tc::Geo<true>::kThreads;
+      out->smem = x3 ? tc::Layout<true, true>::kSmem : tc::Layout<false, true>::kSmem;
+      out->ctas_per_tile_block = 1;
+      return 0;
+    case CWGK_TC_FULL16:
+      out->tiles = tc::Geo<false>::kTiles;
+      out->threads = tc::Geo<false>::kThreads;
+      out->smem = x3 ? tc::Layout<true, false>::kSmem : tc::Layout<false, false>::kSmem;
+      out->ctas_per_tile_block = 1;
+      return 0;
+    default: return -1;
+  }
 }
 
 int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int m, int layout,
                              int from_ref, void *stream) {
-  if (m != 2 || (layout != CWGK_LAYOUT_TC_X3 && layout != CWGK_LAYOUT_TC_X1)) return -2;
+  if (m != 2) return -2;
   const int Cp = (c_in + tc::kCc - 1) / tc::kCc * tc::kCc;
   const int Kp = (c_out + tc::kCout - 1) / tc::kCout * tc::kCout;
   const long total = (long)Cp * Kp;
   const int threads = 256;
   const unsigned blocks = (unsigned)((total + threads - 1) / threads);
   cudaStream_t s = (cudaStream_t)stream;
-  if (layout == CWGK_LAYOUT_TC_X3)
-    tc::wt_transform_tc<true>
-        <<<blocks, threads, 0, s>>>(src, (uint8_t *)U, c_in, c_out, Cp, Kp, from_ref);
-  else
-    tc::wt_transform_tc<false>
-        <<<blocks, threads, 0, s>>>(src, (uint8_t *)U, c_in, c_out, Cp, Kp, from_ref);
+  uint8_t *u = (uint8_t *)U;
+  switch (layout) {
+    case CWGK_LAYOUT_TC_X3:
+      tc::wt_transform_tc<true><<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref);
+      break;
+    case CWGK_LAYOUT_TC_X1:
+      tc::wt_transform_tc<false><<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref);
+      break;
+    case CWGK_LAYOUT_TC2_X3:
+      tc::wt_transform_tc_pair<true>
+          <<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref);
+      break;
+    case CWGK_LAYOUT_TC2_X1:
+      tc::wt_transform_tc_pair<false>
+          <<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref);
+      break;
+    default: return -2;
+  }
   cwgk_count_launch();
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -706,17 +1222,23 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
 }
 
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
-                 int c_out, int h, int w, int x3, int full16, int bf16, int relu, void *stream) {
+                 int c_out, int h, int w, int x3, int variant, int bf16, int relu, void *stream) {
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
 #define CWG_TC_LAUNCH(X3_, HALF_)                                                              \
   (bf16 ? tc::launch<X3_, HALF_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s) \
         : tc::launch<X3_, HALF_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
-  if (x3)
-    e = full16 ? CWG_TC_LAUNCH(true, false) : CWG_TC_LAUNCH(true, true);
-  else
-    e = full16 ? CWG_TC_LAUNCH(false, false) : CWG_TC_LAUNCH(false, true);
+#define CWG_TC_LAUNCH_PAIR(X3_)                                                                 \
+  (bf16 ? tc::launch_pair<X3_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s)    \
+        : tc::launch_pair<X3_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
+  switch (variant) {
+    case CWGK_TC_PAIR: e = x3 ? CWG_TC_LAUNCH_PAIR(true) : CWG_TC_LAUNCH_PAIR(false); break;
+    case CWGK_TC_HALF: e = x3 ? CWG_TC_LAUNCH(true, true) : CWG_TC_LAUNCH(false, true); break;
+    case CWGK_TC_FULL16: e = x3 ? CWG_TC_LAUNCH(true, false) : CWG_TC_LAUNCH(false, false); break;
+    default: return -2;
+  }
 #undef CWG_TC_LAUNCH
+#undef CWG_TC_LAUNCH_PAIR
   cwgk_count_launch();
   if (e != cudaSuccess) {
     cwgk_set_cuda_error((int)e);

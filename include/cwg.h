@@ -52,8 +52,10 @@ extern "C" {
 #define CWG_FORCE_FFMA 0x10u /* ablation: always take the CUDA-core (FFMA) kernel */
 #define CWG_FORCE_TC 0x20u   /* ablation: always take the tcgen05 kernel (EUNSUPPORTED if it cannot) */
 #define CWG_TC_SINGLE 0x40u  /* ablation: fp32 I/O with ONE bf16 product per MAC (below fp32 parity) */
-#define CWG_TC_FULL16 0x80u  /* ablation: tensor-core kernel with all 16 frequency accumulators
-                                (32-tile blocks) instead of the half-folded 8 (64-tile blocks) */
+#define CWG_TC_FULL16 0x80u  /* ablation: single-CTA tensor-core kernel with all 16 frequency
+                                accumulators (32-tile blocks) */
+#define CWG_TC_NOPAIR 0x100u /* ablation: single-CTA half-folded tensor-core kernel (64-tile
+                                blocks) instead of the 2-SM pair kernel (128-tile blocks) */
 
 /* Kernel paths reported by cwg_select. */
 #define CWG_PATH_FFMA 1 /* warp register-blocked FFMA fused kernel */
@@ -63,7 +65,7 @@ extern "C" {
 typedef struct cwg_choice {
   int m;             /* output tile edge: 2 -> F(2x2,3x3), 4 -> F(4x4,3x3) */
   int path;          /* CWG_PATH_* */
-  int tiles_per_cta; /* output tiles one CTA owns */
+  int tiles_per_cta; /* output tiles one CTA owns (one CTA pair, for the 2-SM kernel) */
   int cout_per_cta;  /* output channels one CTA owns */
   int cin_chunk;     /* input channels staged per pipeline step */
   int threads;       /* threads per CTA */

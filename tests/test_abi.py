@@ -88,6 +88,24 @@ def test_weight_bytes():
     assert cwg.weight_bytes(32, 32, 6) == 0
 
 
+def test_selector_tensor_core_variants():
+    n, c, k, h, w = 4, 128, 256, 30, 30
+    tiles = n * 15 * 15
+    pair = cwg.select(n, c, k, h, w)
+    assert pair.path == cwg.PATH_TC and pair.tiles_per_cta == 128 and pair.tmem_cols == 512
+    assert pair.ctas == 2 * (-(-tiles // 128)) * 2  # two CTAs per 128-tile block
+    single = cwg.select(n, c, k, h, w, 2, cwg.TC_NOPAIR)
+    assert single.tiles_per_cta == 64 and single.ctas == (-(-tiles // 64)) * 2
+    assert cwg.select(n, c, k, h, w, 2, cwg.TC_FULL16).tiles_per_cta == 32
+    # the pair layout holds both At-scaled row sets
+    assert cwg.weight_bytes(c, k, 2) == 2 * cwg.weight_bytes(c, k, 2, cwg.TC_NOPAIR)
+    assert cwg.weight_bytes(c, k, 2, cwg.TC_NOPAIR) == 16 * 256 * 128 * 2 * 2
+    assert cwg.weight_bytes(c, k, 2, cwg.BF16) == 16 * 256 * 128 * 2 * 2
+    with pytest.raises(cwg.CwgError) as e:
+        cwg.select(n, c, k, h, w, 2, cwg.TC_NOPAIR | cwg.TC_FULL16)
+    assert e.value.status == cwg.EINVAL
+
+
 def test_layer_call_argument_checks_need_no_gpu():
     L = cwg.lib()
     # NULL pointers / bad sizes are rejected before any CUDA call

@@ -266,6 +266,37 @@ def test_paths_agree(cuda_dev):
         assert_close(y, ref, "f23", f"force={force:#x}")
 
 
+TC_VARIANTS = [0, cwg.TC_NOPAIR, cwg.TC_FULL16]
+
+
+@pytest.mark.parametrize("variant", TC_VARIANTS, ids=["pair", "single", "full16"])
+@pytest.mark.parametrize("case", [(2, 128, 128, 20, 18), (1, 64, 200, 9, 13),
+                                  (3, 96, 128, 7, 7), (1, 256, 64, 3, 33)],
+                         ids=lambda c: "x".join(map(str, c)))
+def test_tensor_core_variants(cuda_dev, case, variant):
+    """Every tcgen05 kernel (2-SM pair, single-CTA half-folded, 16-accumulator)
+    against the reference on ragged shapes: partial channel blocks, tile blocks
+    that cross images, a last block with no valid tile on one CTA of the pair."""
+    n, c, k, h, w = case
+    rng = np.random.default_rng(sum(case) + variant)
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    y = gpu_conv(x, g, bias, 2, cwg.RELU | cwg.FORCE_TC | variant, cuda_dev)
+    assert_close(y, oracle_conv(x, g, bias, 2, True), "f23", f"{case} {variant:#x}")
+
+
+@pytest.mark.parametrize("variant", TC_VARIANTS, ids=["pair", "single", "full16"])
+def test_tensor_core_variants_bf16(cuda_dev, variant):
+    n, c, k, h, w = 2, 128, 192, 14, 14
+    rng = np.random.default_rng(21)
+    x = workloads.bf16_round(rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32))
+    g = workloads.bf16_round(rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32))
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    y = gpu_conv(x, g, bias, 2, cwg.BF16 | cwg.RELU | cwg.FORCE_TC | variant, cuda_dev)
+    assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", f"bf16 {variant:#x}")
+
+
 def test_host_buffer_entry_matches_device_entry(cuda_dev):
     import torch
 
