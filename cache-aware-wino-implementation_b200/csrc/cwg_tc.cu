@@ -1,26 +1,29 @@
-// cwg_tc.cu -- the tcgen05/TMEM fused Winograd F(2x2,3x3) kernel (sm_100a).
+// cwg_tc.cu -- the tcgen05/TMEM fused Winograd F(2x2,3x3) kernels (sm_100a).
 //
-// One CTA computes 128 output channels x 32 output tiles (2x2 pixels each) of
-// one layer:
+// wino_fused_tc_pair (default; defined after the single-CTA kernel): a 2-SM CTA
+// pair computes 128 output channels x 128 output tiles with
+// tcgen05.mma.cta_group::2; see the comment above it.
+//
+// wino_fused_tc (ablations CWG_TC_NOPAIR / CWG_TC_FULL16): one CTA computes 128
+// output channels x 64 (half-folded) or 32 (16 accumulators) output tiles:
 //   * A = U_f   (128 output channels x 16 input channels, bf16, K-major), one
 //                per Winograd frequency f, streamed from global memory by
 //                cp.async.bulk (the weight transform already wrote each
 //                (channel block, 16-channel step, frequency) as the exact
 //                shared-memory image the tensor core reads);
-//   * B = V_f   (32 tiles x 16 input channels, bf16, K-major), written into
-//                shared memory by four transform warps that load the 4x4 input
-//                patches from global memory and compute Bt d B in registers;
-//   * D_f in TMEM: the 16 frequency accumulators (128 lanes x 32 columns each)
-//                fill all 512 columns, so the whole C_in reduction of every
-//                frequency completes on chip;
-//   * epilogue: the same four warps read D (lane = output channel) with
-//                tcgen05.ld, apply At M A, bias and ReLU, and store NCHW.
+//   * B = V_f   (tiles x 16 input channels, bf16, K-major), written into shared
+//                memory by the transform warps, which load the 4x4 input patches
+//                from global memory and compute Bt d B in registers;
+//   * D in TMEM: 8 half-folded or 16 frequency accumulators fill all 512
+//                columns, so the whole C_in reduction completes on chip;
+//   * epilogue: the same warps read D (lane = output channel) with tcgen05.ld,
+//                finish At M A, add bias, apply ReLU and store NCHW.
 // fp32 parity ("x3"): every fp32 operand v is split into hi = bf16(v) and
 // lo = bf16(v - hi); each product runs as three MMAs (hi*hi + hi*lo + lo*hi)
 // into the same fp32 accumulator.  "x1" (bf16 layers) runs one MMA.
 //
-// Warp roles (192 threads): warp 0 allocates TMEM and issues the MMAs from one
-// thread; warp 1 issues the bulk copies of U; warps 2-5 transform and run the
+// Warp roles: warp 0 allocates TMEM and issues the MMAs from one elected lane;
+// warp 1 issues the bulk copies of U; the other warps transform and run the
 // epilogue.  Every mbarrier wait is bounded by %globaltimer: on timeout the
 // kernel sets g_tc_status, drains what it has in flight, frees TMEM and
 // returns, and the host reports CWG_ETIMEOUT.
