@@ -310,9 +310,7 @@ def main() -> None:
         flops_total = layer.conv_flops() * world
         value = flops_total / (t_max * 1e-3) / 1e12
         # roofline of the dominant (conv) kernel, per launch on this GPU
-        products = 1
-        if choice.path == cwg.PATH_TC and not (flags & (cwg.BF16 | cwg.TC_SINGLE)):
-            products = 3
+        products = max(choice.mma_products, 1)
         t_hbm = choice.alg_bytes / (peaks["hbm_gbs"] * 1e9)
         mma_flops = choice.gemm_flops * products
         t_tc = mma_flops / (peaks["bf16_tflops"] * 1e12)

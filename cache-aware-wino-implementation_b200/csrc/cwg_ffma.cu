@@ -18,57 +18,6 @@ static thread_local int t_cuda_error = 0;
 // ============================================================================
 // Weight transform
 // ============================================================================
-// G for F(2,3) and F(4,3): the unique matrices that make the reference's Bt/At
-// (src/fused_winograd_kernel.py:18-46) compute a 3x3 cross-correlation.
-template <int M>
-__device__ __forceinline__ double gmat(int a, int i);
-template <>
-__device__ __forceinline__ double gmat<2>(int a, int i) {
-  const double g[4][3] = {{1, 0, 0}, {.5, .5, .5}, {.5, -.5, .5}, {0, 0, 1}};
-  return g[a][i];
-}
-template <>
-__device__ __forceinline__ double gmat<4>(int a, int i) {
-  const double g[6][3] = {{1. / 4, 0, 0},          {-1. / 6, -1. / 6, -1. / 6},
-                          {-1. / 6, 1. / 6, -1. / 6}, {1. / 24, 1. / 12, 1. / 6},
-                          {1. / 24, -1. / 12, 1. / 6}, {0, 0, 1}};
-  return g[a][i];
-}
-
-// u[f] for one (k, c) pair, in fp64 with the same operation order as the CPU
-// oracle (no contraction), rounded once to fp32.
-template <int M>
-__device__ __forceinline__ void transform_one(const float *src, int from_ref, float *u) {
-  constexpr int TD = M + 2, NF = TD * TD;
-  if (from_ref) {
-#pragma unroll
-    for (int f = 0; f < NF; ++f) u[f] = src[f];
-    return;
-  }
-  double gk[9];
-#pragma unroll
-  for (int i = 0; i < 9; ++i) gk[i] = (double)src[i];
-  double t[TD][3];
-#pragma unroll
-  for (int a = 0; a < TD; ++a)
-#pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      double s = 0.0;
-#pragma unroll
-      for (int i = 0; i < 3; ++i) s = __dadd_rn(s, __dmul_rn(gmat<M>(a, i), gk[i * 3 + j]));
-      t[a][j] = s;
-    }
-#pragma unroll
-  for (int a = 0; a < TD; ++a)
-#pragma unroll
-    for (int b = 0; b < TD; ++b) {
-      double s = 0.0;
-#pragma unroll
-      for (int j = 0; j < 3; ++j) s = __dadd_rn(s, __dmul_rn(t[a][j], gmat<M>(b, j)));
-      u[a * TD + b] = (float)s;
-    }
-}
-
 // One thread per (c, k); k fastest so the [f][C][K] stores coalesce.
 template <int M>
 __global__ void wt_transform_ffma(const float *__restrict__ src, float *__restrict__ U, int C,

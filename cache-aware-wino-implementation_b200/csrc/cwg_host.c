@@ -78,11 +78,6 @@ static int num_sms(void) {
 
 /* ---- path decision (depends only on c_in, c_out, m, flags, so that the
  * weight layout chosen at transform time matches the conv call) ----------- */
-static int tc_available(int x3) {
-  cwgk_tc_cfg cfg;
-  return cwgk_tc_get_cfg(x3, CWGK_TC_PAIR, &cfg) == 0;
-}
-
 /* Tensor-core kernel variant: the 2-SM pair kernel unless a flag asks for one
  * of the single-CTA kernels. */
 static int tc_variant(unsigned flags) {
@@ -91,8 +86,28 @@ static int tc_variant(unsigned flags) {
   return CWGK_TC_PAIR;
 }
 
+/* Products per multiply-accumulate on the tensor cores: 3 (bf16 hi/lo split,
+ * fp32-accurate) for fp32 layers and for bf16 F(4,3) layers -- F(4,3)'s output
+ * transform (coefficients up to 8) turns single bf16 products into ~6% errors
+ * -- and 1 for bf16 F(2,3) layers or when CWG_TC_SINGLE asks for it. */
+static int tc_x3(int m, unsigned flags) {
+  if (flags & CWG_TC_SINGLE) return 0;
+  if (flags & CWG_BF16) return m == 4;
+  return 1;
+}
+
+/* F(4,3) runs on the tensor cores for bf16 layers only: with fp32 data the
+ * hi/lo split's dropped lo*lo terms, amplified by the output transform, leave
+ * ~4e-4 absolute error against fp32 F(4,3) -- outside the fp32 parity bar. */
+static int tc_available(int m, unsigned flags) {
+  cwgk_tc_cfg cfg;
+  if (m == 4 && !(flags & CWG_BF16)) return 0;
+  return cwgk_tc_get_cfg(tc_x3(m, flags), tc_variant(flags), m, &cfg) == 0;
+}
+
 /* Tensor cores only where the per-frequency GEMM is a real contraction: both
- * channel counts >= 64 (the kernel zero-pads C_in to 16 and C_out to 128). */
+ * channel counts >= 64 (the kernels zero-pad C_in to 16 and C_out to the
+ * channel block). */
 static int tc_shape_ok(int c_in, int c_out) { return c_in >= 64 && c_out >= 64; }
 
 /* Resolves m and the path; returns CWG_OK or an error. */
@@ -101,16 +116,17 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
   if (m != 0 && m != 2 && m != 4) return (m == 6) ? CWG_EUNSUPPORTED : CWG_EINVAL;
   if ((flags & CWG_FORCE_FFMA) && (flags & CWG_FORCE_TC)) return CWG_EINVAL;
   if ((flags & CWG_TC_FULL16) && (flags & CWG_TC_NOPAIR)) return CWG_EINVAL;
-  const int x3 = !(flags & (CWG_BF16 | CWG_TC_SINGLE));
-  const int tc_ok = tc_available(x3) && tc_shape_ok(c_in, c_out) && (m == 0 || m == 2);
+  /* the tensor-core path runs F(2,3) unless F(4,3) is asked for */
+  const int m_tc = m ? m : 2;
+  const int tc_ok = tc_shape_ok(c_in, c_out) && tc_available(m_tc, flags);
   if (flags & CWG_FORCE_TC) {
     if (!tc_ok) return CWG_EUNSUPPORTED;
-    *m_out = 2;
+    *m_out = m_tc;
     *path_out = CWG_PATH_TC;
     return CWG_OK;
   }
   if (!(flags & CWG_FORCE_FFMA) && tc_ok) {
-    *m_out = 2;
+    *m_out = m_tc;
     *path_out = CWG_PATH_TC;
     return CWG_OK;
   }
@@ -123,11 +139,11 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
   return CWG_OK;
 }
 
-static int layout_of(int path, unsigned flags) {
+static int layout_of(int path, int m, unsigned flags) {
   if (path == CWG_PATH_TC) {
-    const int x1 = (flags & (CWG_BF16 | CWG_TC_SINGLE)) != 0;
-    if (tc_variant(flags) == CWGK_TC_PAIR) return x1 ? CWGK_LAYOUT_TC2_X1 : CWGK_LAYOUT_TC2_X3;
-    return x1 ? CWGK_LAYOUT_TC_X1 : CWGK_LAYOUT_TC_X3;
+    const int x3 = tc_x3(m, flags);
+    if (tc_variant(flags) == CWGK_TC_PAIR) return x3 ? CWGK_LAYOUT_TC2_X3 : CWGK_LAYOUT_TC2_X1;
+    return x3 ? CWGK_LAYOUT_TC_X3 : CWGK_LAYOUT_TC_X1;
   }
   /* The CUDA-core kernel keeps U in fp32 for bf16 layers too: rounding U to
    * bf16 loses ~4% through F(4,3)'s output transform (coefficients up to 8). */
@@ -142,10 +158,14 @@ static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
     case CWGK_LAYOUT_TC_X1:
     case CWGK_LAYOUT_TC2_X3:
     case CWGK_LAYOUT_TC2_X1: {
-      const size_t kp = ((size_t)c_out + 127) / 128 * 128;
+      const int pair = layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
+      /* output channels per weight block: 128 rows hold m/2 output rows of
+       * channels in the pair layout */
+      const size_t kb = pair ? (size_t)(128 / (m / 2)) : 128;
+      const size_t kp = ((size_t)c_out + kb - 1) / kb * kb;
       const size_t cp = ((size_t)c_in + 15) / 16 * 16;
       const size_t parts = (layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3) ? 2 : 1;
-      const size_t sets = (layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1) ? 2 : 1;
+      const size_t sets = pair ? 2 : 1;
       return nf * kp * cp * 2 * parts * sets;
     }
     default: return 0;
@@ -193,12 +213,12 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
   const int esz = (flags & CWG_BF16) ? 2 : 4;
   out->gemm_flops = 2.0 * (double)n * th * tw * c_out * c_in * td2;
   out->alg_bytes = (double)n * c_in * h * w * esz + (double)n * c_out * h * w * esz +
-                   (double)weight_bytes_for(c_in, c_out, mm, layout_of(path, flags)) +
+                   (double)weight_bytes_for(c_in, c_out, mm, layout_of(path, mm, flags)) +
                    4.0 * c_out;
   if (path == CWG_PATH_TC) {
     cwgk_tc_cfg t;
-    const int lay = layout_of(path, flags);
-    cwgk_tc_get_cfg(lay == CWGK_LAYOUT_TC_X3 || lay == CWGK_LAYOUT_TC2_X3, tc_variant(flags), &t);
+    cwgk_tc_get_cfg(tc_x3(mm, flags), tc_variant(flags), mm, &t);
+    out->mma_products = tc_x3(mm, flags) ? 3 : 1;
     out->tiles_per_cta = t.tiles;
     out->cout_per_cta = t.kb;
     out->cin_chunk = t.cc;
@@ -226,7 +246,7 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
 size_t cwg_weight_bytes(int c_in, int c_out, int m, unsigned flags) {
   int mm = 0, path = 0;
   if (decide(c_in, c_out, m, flags, &mm, &path)) return 0;
-  return weight_bytes_for(c_in, c_out, mm, layout_of(path, flags));
+  return weight_bytes_for(c_in, c_out, mm, layout_of(path, mm, flags));
 }
 
 static int weight_common(const float *src, void *U, int c_in, int c_out, int m, unsigned flags,
@@ -237,7 +257,7 @@ static int weight_common(const float *src, void *U, int c_in, int c_out, int m, 
   const int rc = decide(c_in, c_out, m, flags, &mm, &path);
   if (rc) return rc;
   if (from_ref && m == 0) return CWG_EINVAL; /* a reference-layout U fixes td */
-  return cwgk_weight_transform(src, U, c_in, c_out, mm, layout_of(path, flags), from_ref,
+  return cwgk_weight_transform(src, U, c_in, c_out, mm, layout_of(path, mm, flags), from_ref,
                                stream);
 }
 
@@ -267,10 +287,8 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   const int relu = (flags & CWG_RELU) ? 1 : 0;
   const int bf16 = (flags & CWG_BF16) ? 1 : 0;
   if (path == CWG_PATH_TC) {
-    const int lay = layout_of(path, flags);
-    const int x3 = lay == CWGK_LAYOUT_TC_X3 || lay == CWGK_LAYOUT_TC2_X3;
-    return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, x3, tc_variant(flags), bf16, relu,
-                        stream);
+    return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, mm, tc_x3(mm, flags),
+                        tc_variant(flags), bf16, relu, stream);
   }
   cwgk_ffma_cfg cfg;
   const int idx = pick_ffma(n, c_out, h, w, mm, &cfg);

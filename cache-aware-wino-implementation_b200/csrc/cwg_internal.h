@@ -17,13 +17,13 @@ enum {
   CWGK_LAYOUT_FFMA_F32 = 1,  /* fp32 [td*td][C_in][C_out] (fp32 and bf16 layers)  */
   CWGK_LAYOUT_TC_X3 = 3,     /* bf16 hi+lo UMMA blocks (fp32-parity tensor path)  */
   CWGK_LAYOUT_TC_X1 = 4,     /* bf16 UMMA blocks (single product)                 */
-  CWGK_LAYOUT_TC2_X3 = 5,    /* pair kernel: At-scaled hi+lo blocks, 2 row sets   */
+  CWGK_LAYOUT_TC2_X3 = 5,    /* pair kernel: At-scaled hi+lo blocks, 2 rank sets  */
   CWGK_LAYOUT_TC2_X1 = 6     /* pair kernel: At-scaled blocks, single product     */
 };
 
 /* Tensor-core kernel variants. */
 enum {
-  CWGK_TC_PAIR = 0,   /* 2-SM pair, M = 256 (both output-row parities), N = 128 */
+  CWGK_TC_PAIR = 0,   /* 2-SM pair, M = 256 (stacked output rows), F(2,3) and F(4,3) */
   CWGK_TC_HALF = 1,   /* one CTA, half-folded, M = 128, N = 64                  */
   CWGK_TC_FULL16 = 2  /* one CTA, 16 frequency accumulators, N = 32             */
 };
@@ -52,7 +52,7 @@ typedef struct cwgk_tc_cfg {
 
 int cwgk_ffma_num_cfgs(void);
 int cwgk_ffma_get_cfg(int idx, cwgk_ffma_cfg *out);
-int cwgk_tc_get_cfg(int x3, int variant, cwgk_tc_cfg *out);
+int cwgk_tc_get_cfg(int x3, int variant, int m, cwgk_tc_cfg *out);
 
 /* g (or U_ref when from_ref) -> U in `layout`.  Device pointers. */
 int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m, int layout,
@@ -66,10 +66,12 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
 int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
                    int c_in, int c_out, int h, int w, int bf16, int relu, void *stream);
 
-/* tcgen05 fused convolution, F(2,3) (C_in padded to 16, C_out to 128 by the
- * weight layout), kernel `variant` (CWGK_TC_*). */
+/* tcgen05 fused convolution F(m x m, 3x3) (C_in padded to 16 and C_out to the
+ * channel block by the weight layout), kernel `variant` (CWGK_TC_*; the
+ * single-CTA variants are F(2,3) only). */
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
-                 int c_out, int h, int w, int x3, int variant, int bf16, int relu, void *stream);
+                 int c_out, int h, int w, int m, int x3, int variant, int bf16, int relu,
+                 void *stream);
 
 /* Per-tile kernel on device buffers (reference layouts). */
 int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,

@@ -666,16 +666,18 @@ static cudaError_t launch(const void *x, const void *U, const float *bias, void 
 
 // ==== 2-SM pair kernel (tcgen05.mma.cta_group::2) ====================================
 //
-// A CTA pair (a cluster of two, on the two SMs of one TPC) computes 128 output
-// channels x 128 tiles.  The half-folded accumulation is stacked along M:
-//   A (M = 256) = [At[0][a] U_ab ; At[1][a] U_ab]  -- rank r holds the 128 rows of
-//                 output-row parity i = r, pre-scaled by At (0 / +-1, exact);
-//   B (N = 128) = V_ab of the pair's 128 tiles     -- rank r holds tiles 64r..64r+63;
-//   D           = Z[i][b] = sum_a At[i][a] M[a][b] -- 4 accumulators x 128 tiles
-//                 per CTA: rank r's TMEM holds output row 2ty + r of every tile.
-// One MMA per (frequency, product) now serves both output rows and 128 tiles:
-// per SM the tensor core reads 6 KB of shared memory per 262K MACs instead of
-// 6 KB per 131K, and each CTA streams its weights once per 128 tiles.
+// A CTA pair (a cluster of two, on the two SMs of one TPC) computes one block
+// of output channels x N tiles.  The half-folded accumulation
+// Z[i][b] = sum_a At[i][a] M[a][b] is stacked along M = 256:
+//   A = [At[0][a] U_ab ; ... ; At[m-1][a] U_ab]  -- the rows of every output-row
+//        index i, pre-scaled by At (exact in bf16); rank r holds 128 of them;
+//   B = V_ab of the pair's N tiles               -- rank r holds half of them;
+//   D = Z[i][b]: rank r's TMEM holds, for its rows, (m+2) accumulators x N.
+// F(2,3): 128 channels x 128 tiles, rank r = output row 2ty + r.  F(4,3): 64
+// channels x 64 tiles, rank r = output rows 4ty + 2r, 4ty + 2r + 1.  One MMA
+// per (frequency, product) serves every output row and N tiles: for F(2,3) the
+// tensor core reads 6 KB of shared memory per 262K MACs of an SM instead of
+// 6 KB per 131K in the single-CTA kernel.
 //
 // Rank 0 issues every MMA and commit for the pair.  Readiness of rank 1's
 // operands reaches rank 0 by remote mbarrier arrivals: rank 1's warp 0 (idle
@@ -738,77 +740,91 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
 }
 
-// Pair weight layout: [K_pad/128][i = 2][C_pad/16][16 f][parts][4096 B block];
-// block (k, c) of frequency f = (a, b) holds At[i][a] * U_ab (sign flips and
-// zeros are exact in bf16).  Channels past C_out / C_in are zero.
-template <bool X3>
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[e]);
+}
+
+// Geometry of the pair kernel for F(M x M, 3x3).
+//   F(2,3): rank r holds the 128 rows (i = r, output channel), 64 tiles of V;
+//           N = 128, 4 accumulators Z[r][b] x 128 columns.
+//   F(4,3): rank r holds 2 x 64 rows (i = 2r + il, output channel), 32 tiles
+//           of V; N = 64, 6 accumulators x 64 columns.
+template <int M>
+struct PairGeo {
+  static constexpr int TD = M + 2, NF = TD * TD;
+  static constexpr int kRowsI = M / 2;              // output rows i per CTA
+  static constexpr int kCoutCta = kCout / kRowsI;   // output channels per CTA
+  static constexpr int kTiles = M == 2 ? 64 : 32;   // V columns (tiles) per CTA
+  static constexpr int kN = 2 * kTiles;             // MMA N of the pair
+  static constexpr int kXWarps = 16;                // transform + epilogue warps
+  static constexpr int kThreads = (2 + kXWarps) * 32;
+  // F(4,3): two groups of 8 warps transform alternate stages (a 6x6 window
+  // for two channels leaves no registers for a prefetched next stage).
+  static constexpr int kGroups = M == 2 ? 1 : 2;
+  static constexpr int kGroupWarps = kXWarps / kGroups;
+  static constexpr int kNU = M == 2 ? 5 : 4;        // weight stages
+  static constexpr int kVBytes = kTiles * kCc * 2;  // one frequency of V
+  static constexpr int kEpiTiles = 32 / M;          // tiles per 32-pixel epilogue row
+  static_assert(TD * kN <= kTmemCols, "accumulators fit TMEM");
+  static_assert(kTiles * 8 == kGroupWarps * 32, "one (tile, channel pair) per thread");
+};
+
+// Pair weight layout: [ceil(C_out/cout_cta)][rank = 2][C_pad/16][NF f][parts][4096 B]:
+// block row il * cout_cta + k' of rank r holds At[r * rows_i + il][a] * U_ab for
+// output channel kblk * cout_cta + k' (scaling by 0, +-1, +-2, +-4, +-8 is exact
+// in bf16).  Channels past C_out / C_in are zero.
+template <int M, bool X3>
 __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__restrict__ U,
                                      int C, int K, int Cp, int Kp, int from_ref) {
+  using G = PairGeo<M>;
+  constexpr int NF = G::NF, TD = G::TD;
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)Cp * Kp) return;
   const int c = (int)(idx % Cp), k = (int)(idx / Cp);
-  float u[kNF];
+  float u[NF];
   if (k < K && c < C) {
-    if (from_ref) {
-#pragma unroll
-      for (int f = 0; f < kNF; ++f) u[f] = src[((long)k * C + c) * kNF + f];
-    } else {
-      // fp64 G g G^T, same operation order as the CPU oracle, rounded once
-      const double G[4][3] = {{1, 0, 0}, {.5, .5, .5}, {.5, -.5, .5}, {0, 0, 1}};
-      const float *g = src + ((long)k * C + c) * 9;
-      double t[4][3];
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int j = 0; j < 3; ++j) {
-          double s = 0.0;
-#pragma unroll
-          for (int i = 0; i < 3; ++i) s = __dadd_rn(s, __dmul_rn(G[a][i], (double)g[i * 3 + j]));
-          t[a][j] = s;
-        }
-#pragma unroll
-      for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          double s = 0.0;
-#pragma unroll
-          for (int j = 0; j < 3; ++j) s = __dadd_rn(s, __dmul_rn(t[a][j], G[b][j]));
-          u[a * 4 + b] = (float)s;
-        }
-    }
+    transform_one<M>(src + ((long)k * C + c) * (from_ref ? NF : 9), from_ref, u);
   } else {
 #pragma unroll
-    for (int f = 0; f < kNF; ++f) u[f] = 0.f;
+    for (int f = 0; f < NF; ++f) u[f] = 0.f;
   }
   constexpr int parts = X3 ? 2 : 1;
   const int C16 = Cp / kCc;
-  const uint32_t off = blk_off(k % kCout, c % kCc);
+  const int kb = k / G::kCoutCta, kr = k % G::kCoutCta;
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const long blk0 = ((long)(k / kCout) * 2 + i) * C16 + c / kCc;
+  for (int r = 0; r < 2; ++r)
 #pragma unroll
-    for (int f = 0; f < kNF; ++f) {
-      const int sgn = at23(i, f >> 2);
-      const __nv_bfloat16 hi = __float2bfloat16_rn(u[f]);
-      const __nv_bfloat16 lo = __float2bfloat16_rn(u[f] - __bfloat162float(hi));
-      const __nv_bfloat16 z = __float2bfloat16_rn(0.f);
-      uint8_t *b = U + ((blk0 * kNF + f) * parts) * kCoreBytes;
-      *reinterpret_cast<__nv_bfloat16 *>(b + off) = sgn == 0 ? z : (sgn < 0 ? __hneg(hi) : hi);
-      if (X3)
-        *reinterpret_cast<__nv_bfloat16 *>(b + kCoreBytes + off) =
-            sgn == 0 ? z : (sgn < 0 ? __hneg(lo) : lo);
+    for (int il = 0; il < G::kRowsI; ++il) {
+      const long blk0 = ((long)kb * 2 + r) * C16 + c / kCc;
+      const uint32_t off = blk_off(il * G::kCoutCta + kr, c % kCc);
+#pragma unroll
+      for (int f = 0; f < NF; ++f) {
+        const float s = Wino<M>::at(r * G::kRowsI + il, f / TD) * u[f];
+        const __nv_bfloat16 hi = __float2bfloat16_rn(s);
+        uint8_t *b = U + ((blk0 * NF + f) * parts) * kCoreBytes;
+        *reinterpret_cast<__nv_bfloat16 *>(b + off) = hi;
+        if (X3)
+          *reinterpret_cast<__nv_bfloat16 *>(b + kCoreBytes + off) =
+              __float2bfloat16_rn(s - __bfloat162float(hi));
+      }
     }
-  }
 }
 
-// Shared memory of one CTA of the pair: the operand rings of the half-folded
-// single-CTA kernel plus the relay barriers.
-template <bool X3>
+// Shared memory of one CTA of the pair.
+template <int M, bool X3>
 struct PairLayout {
-  using G = Geo<true>;
+  using G = PairGeo<M>;
   static constexpr int kNU = G::kNU;
   static constexpr int kParts = X3 ? 2 : 1;
-  static constexpr int kVStage = kParts * kNF * G::kVBytes;     // 64 tiles
+  static constexpr int kVStage = kParts * G::NF * G::kVBytes;
   static constexpr int kUStage = kFPerU * kParts * kCoreBytes;
   static constexpr int kVOff = 0;
   static constexpr int kUOff = kVOff + kNV * kVStage;
@@ -824,21 +840,21 @@ struct PairLayout {
   // the patches reuse the operand rings once every MMA has completed
   static_assert(G::kXWarps * kPatchFloats * 4 <= kBarOff, "patches fit the operand rings");
   static_assert(kSmem <= 227 * 1024, "fits the opt-in shared memory of one CTA");
+  static_assert(G::NF % kFPerU == 0, "whole frequencies per weight stage");
 };
 
-constexpr int kPairTiles = 128;  // MMA N of the pair (64 tiles per CTA)
-
-template <bool X3, typename Tio>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads, 1)
+template <int M, bool X3, typename Tio>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads, 1)
     wino_fused_tc_pair(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                        const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
                        int W, int tiles_y, int tiles_x, long long total_tiles, int relu) {
-  using L = PairLayout<X3>;
-  using G = Geo<true>;
-  constexpr int P = L::kParts;
-  constexpr int kTiles = G::kTiles, kNU = L::kNU, kVBytes = G::kVBytes;
+  using L = PairLayout<M, X3>;
+  using G = PairGeo<M>;
+  constexpr int P = L::kParts, TD = G::TD, NF = G::NF;
+  constexpr int kTiles = G::kTiles, kN = G::kN, kNU = L::kNU, kVBytes = G::kVBytes;
   constexpr int kXW = G::kXWarps;
   constexpr int kEpiThreads = 32 * kXW;
+  constexpr int kUPerStage = NF / kFPerU;  // weight stages per 16-channel stage
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const uint32_t v_full = sbase + L::kBarOff, v_empty = v_full + 8 * kNV;
@@ -851,15 +867,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
 
   const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0);  // warp-uniform
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_rank();  // 0: issues the MMAs; also the output-row parity
+  const uint32_t rank = cluster_rank();  // 0: issues the MMAs
   const int C16 = (C + kCc - 1) / kCc;
   const int kblk = blockIdx.y;
-  const long long pair0 = (long long)(blockIdx.x >> 1) * kPairTiles;  // first tile of the pair
-  const long long tile0 = pair0 + (long long)rank * kTiles;          // this CTA's V columns
+  const long long pair0 = (long long)(blockIdx.x >> 1) * kN;  // first tile of the pair
+  const long long tile0 = pair0 + (long long)rank * kTiles;  // this CTA's V columns
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNV; ++i) {
-      mbar_init(v_full + 8 * i, kXW);
+      mbar_init(v_full + 8 * i, G::kGroupWarps);
       mbar_init(v_empty + 8 * i, 1);
       mbar_init(v_peer + 8 * i, 1);
     }
@@ -887,10 +903,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
     named_bar_arrive(kBarTmem, 32 + kEpiThreads);
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int nstages = C16 * (kNF / kFPerU);
     if (rank == 0) {
-      constexpr uint32_t idesc = instr_desc(2 * kCout, kPairTiles);
-      constexpr uint32_t kLo = (uint32_t)(kNF * kVBytes) >> 4;  // V hi -> V lo
+      constexpr uint32_t idesc = instr_desc(2 * kCout, kN);
+      constexpr uint32_t kLo = (uint32_t)(NF * kVBytes) >> 4;  // V hi -> V lo
       const uint64_t a0 = smem_desc(sbase + L::kUOff, 128, 256);
       const uint64_t b0 = smem_desc(sbase + L::kVOff, (uint32_t)(kTiles * 16), 128);
       bool ok = true;
@@ -902,8 +917,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
         if (!ok) break;
         tc_fence_after();
         const uint64_t bst = b0 + (uint64_t)((uint32_t)(vs * L::kVStage) >> 4);
-#pragma unroll
-        for (int fp = 0; fp < kNF / kFPerU; ++fp, ++ui) {
+#pragma unroll 2
+        for (int fp = 0; fp < kUPerStage; ++fp, ++ui) {
           const int us = ui % kNU;
           const uint32_t ph = (ui / kNU) & 1;
           ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, ph, abort) &&
@@ -916,9 +931,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
             const int f = fp * kFPerU + fi;
             const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * kCoreBytes) >> 4);
             const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
-            // accumulator Z[.][b]; its first term is a = 0 of the first stage
-            const uint32_t d = tmem + (uint32_t)((f & 3) * kPairTiles);
-            const uint32_t first = (cs > 0 || f >= 4) ? 1u : 0u;
+            // accumulator Z[.][b], b = f % TD; its first term is a = 0 of stage 0
+            const uint32_t d = tmem + (uint32_t)((f % TD) * kN);
+            const uint32_t first = (cs > 0 || f >= TD) ? 1u : 0u;
             if (elect_one()) mma_pair_bf16(d, ah, bh, idesc, first);
             if (X3) {
               if (elect_one()) mma_pair_bf16(d, ah, bh + kLo, idesc, 1u);
@@ -948,7 +963,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
     } else {
       // relay, in the order rank 0 consumes them: each V stage written and each
       // weight stage landed here -> one arrival on rank 0's barrier.
-      (void)nstages;
       const uint32_t v_peer_r0 = mapa_shared(v_peer, 0), u_peer_r0 = mapa_shared(u_peer, 0);
       int ui = 0;
       bool ok = true;
@@ -958,7 +972,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
         if (!ok) break;
         if (elect_one()) mbar_arrive_cluster(v_peer_r0 + 8 * vs);
         __syncwarp();
-        for (int fp = 0; fp < kNF / kFPerU; ++fp, ++ui) {
+        for (int fp = 0; fp < kUPerStage; ++fp, ++ui) {
           const int us = ui % kNU;
           ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, (ui / kNU) & 1, abort));
           if (!ok) break;
@@ -969,13 +983,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
     }
   } else if (warp == 1) {
     // ---------------- producer: this CTA's weight rows by bulk copy ----------------
-    const int nstages = C16 * (kNF / kFPerU);
-    const uint8_t *ublk = U + ((size_t)kblk * 2 + rank) * C16 * kNF * P * kCoreBytes;
+    const int nstages = C16 * kUPerStage;
+    const uint8_t *ublk = U + ((size_t)kblk * 2 + rank) * C16 * NF * P * kCoreBytes;
     int issued = 0;
     for (int i = 0; i < nstages; ++i) {
       const int s = i % kNU;
-      if (!__all_sync(0xffffffffu,
-                        mbar_wait(u_empty + 8 * s, ((i / kNU) & 1) ^ 1, abort)))
+      if (!__all_sync(0xffffffffu, mbar_wait(u_empty + 8 * s, ((i / kNU) & 1) ^ 1, abort)))
         break;
       if (elect_one()) {
         mbar_expect_tx(u_full + 8 * s, L::kUStage);
@@ -992,14 +1005,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
       }
     }
   } else {
-    // ---------------- transform warps (this CTA's 64 tiles), then epilogue ----------
+    // ---------------- transform warps (this CTA's tiles), then epilogue ----------
     const int tw = warp - 2;
-    constexpr int kTileBlocks = kTiles / 16, CPT = G::kCpt;
-    static_assert(CPT == 2, "two channels per transform thread");
-    const int cgrp = tw / kTileBlocks;
-    const int cbase = cgrp * (2 * CPT) + (lane & 1) * CPT;
+    const int grp = tw / G::kGroupWarps, gw = tw % G::kGroupWarps;
+    // warp -> (16-tile block, 4 channels); lane -> (tile, channel pair)
+    constexpr int kTileBlocks = kTiles / 16;
+    const int cgrp = gw / kTileBlocks;
+    const int cbase = cgrp * 4 + (lane & 1) * 2;
     const int kh = cbase >> 3;
-    const int t = (tw % kTileBlocks) * 16 + (lane >> 1);
+    const int t = (gw % kTileBlocks) * 16 + (lane >> 1);
     const long long T = tile0 + t;
     const bool tile_ok = T < total_tiles;
     int n = 0, ty = 0, tx = 0;
@@ -1010,107 +1024,170 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
       ty = rem / tiles_x;
       tx = rem - ty * tiles_x;
     }
-    const int y0 = 2 * ty - 1, x0 = 2 * tx - 1;
+    const int y0 = M * ty - 1, x0 = M * tx - 1;
     const size_t plane = (size_t)H * W;
     const Tio *xn = x + (size_t)n * C * plane;
-    bool rv[4], cv[4];
+    bool rv[TD], cv[TD];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < TD; ++i) {
       rv[i] = tile_ok && (y0 + i) >= 0 && (y0 + i) < H;
       cv[i] = (x0 + i) >= 0 && (x0 + i) < W;
     }
-    float d[CPT][4][4];
+    float d[2][TD][TD];  // [channel][row][col]
     auto load_stage = [&](int cs) {
 #pragma unroll
-      for (int q = 0; q < CPT; ++q) {
+      for (int q = 0; q < 2; ++q) {
         const int c = cs * kCc + cbase + q;
         const bool cok = c < C;
         const Tio *xc = xn + (size_t)c * plane;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < TD; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
+          for (int j = 0; j < TD; ++j)
             d[q][i][j] = (cok && rv[i] && cv[j])
                              ? to_f32(xc[(size_t)(y0 + i) * W + (x0 + j)])
                              : 0.f;
       }
     };
-    bool ok = true;
-    if (C16 > 0) load_stage(0);
-    for (int cs = 0; cs < C16; ++cs) {
-      const int vs = cs % kNV;
-      ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
-      if (!ok) break;
-      uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
+    // V of frequency f, channels (cbase, cbase+1) of tile t: 4 bytes per part
+    auto put_v = [&](uint8_t *vb, int f, float e0, float e1) {
       const uint32_t off = (uint32_t)(kh * (kTiles * 16) + t * 16 + (cbase & 7) * 2);
-      float v[CPT][4][4];
-#pragma unroll
-      for (int q = 0; q < CPT; ++q) input_transform<2>(d[q], v[q]);
-#pragma unroll
-      for (int f = 0; f < kNF; ++f) {
-        const int a = f >> 2, b = f & 3;
-        const float e0 = v[0][a][b], e1 = v[1][a][b];
-        uint32_t hi, lo;
-        if (X3) {
-          split_pair(e0, e1, hi, lo);
-          *reinterpret_cast<uint32_t *>(vb + (kNF + f) * kVBytes + off) = lo;
-        } else {
-          hi = pack_bf16(e0, e1);
-        }
-        *reinterpret_cast<uint32_t *>(vb + f * kVBytes + off) = hi;
+      uint32_t hi, lo;
+      if (X3) {
+        split_pair(e0, e1, hi, lo);
+        *reinterpret_cast<uint32_t *>(vb + (NF + f) * kVBytes + off) = lo;
+      } else {
+        hi = pack_bf16(e0, e1);
       }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(v_full + 8 * vs);
-      if (cs + 1 < C16) load_stage(cs + 1);
+      *reinterpret_cast<uint32_t *>(vb + f * kVBytes + off) = hi;
+    };
+    bool ok = true;
+    if constexpr (M == 2) {
+      // every warp takes every stage; the next stage's patches load during this one
+      if (C16 > 0) load_stage(0);
+      for (int cs = 0; cs < C16; ++cs) {
+        const int vs = cs % kNV;
+        ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
+        if (!ok) break;
+        uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
+        float v[2][TD][TD];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) input_transform<M>(d[q], v[q]);
+#pragma unroll
+        for (int f = 0; f < NF; ++f) put_v(vb, f, v[0][f / TD][f % TD], v[1][f / TD][f % TD]);
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(v_full + 8 * vs);
+        if (cs + 1 < C16) load_stage(cs + 1);
+      }
+    } else {
+      // group g takes the stages cs = g (mod 2), i.e. always V slot g.  Bt d Bt^T:
+      // the row pass runs in place, then each output row a is formed, packed and
+      // stored, so two 6x6 windows fit the register budget.
+      for (int cs = grp; cs < C16; cs += G::kGroups) {
+        const int vs = cs % kNV;
+        ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
+        if (!ok) break;
+        load_stage(cs);
+        uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+#pragma unroll
+          for (int i = 0; i < TD; ++i) {
+            float w[TD];
+#pragma unroll
+            for (int b = 0; b < TD; ++b) {
+              float s = 0.f;
+#pragma unroll
+              for (int j = 0; j < TD; ++j) {
+                const float cf = Wino<M>::bt(b, j);
+                if (cf != 0.f) s = fmaf(cf, d[q][i][j], s);
+              }
+              w[b] = s;
+            }
+#pragma unroll
+            for (int b = 0; b < TD; ++b) d[q][i][b] = w[b];
+          }
+#pragma unroll
+        for (int a = 0; a < TD; ++a)
+#pragma unroll
+          for (int b = 0; b < TD; ++b) {
+            float e[2];
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              float s = 0.f;
+#pragma unroll
+              for (int i = 0; i < TD; ++i) {
+                const float cf = Wino<M>::bt(a, i);
+                if (cf != 0.f) s = fmaf(cf, d[q][i][b], s);
+              }
+              e[q] = s;
+            }
+            put_v(vb, a * TD + b, e[0], e[1]);
+          }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(v_full + 8 * vs);
+      }
     }
 
-    // ---------------- epilogue: output row 2ty + rank of the pair's 128 tiles ----------
+    // ---------------- epilogue: output rows M ty + i of the pair's tiles ----------
     named_bar_sync(kBarTmem, 32 + kEpiThreads);
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort));
     tc_fence_after();
     if (ok) {
-      // Lane = output channel after tcgen05.ld.  Each group of 16 tiles (32
-      // output pixels of one row parity) goes through a private patch (row
-      // stride 33 floats) so that a warp store writes one contiguous 128-byte
-      // row segment of one channel plane.  Every MMA has completed and every
+      // TMEM lane = (il, output channel).  Each group of kEpiTiles tiles (32
+      // output pixels of one row) goes through a private patch (row stride 33
+      // floats) so that a warp store writes one contiguous 128-byte row
+      // segment of one channel plane.  Every MMA has completed and every
       // weight copy landed: the operand rings of this CTA are free.
+      constexpr int kE = G::kEpiTiles;
       const int quad = warp & 3;
-      const int col0 = (tw >> 2) * (kPairTiles / 4);  // 32 tiles per warp
-      const int kq = kblk * kCout + quad * 32;
+      const int il = (quad * 32) / G::kCoutCta;
+      const int irow = (int)rank * G::kRowsI + il;  // output row i of the tile
+      const int col0 = (tw >> 2) * (kN / 4);        // 32 (F2) or 16 (F4) tiles per warp
+      const int kq = kblk * G::kCoutCta + (quad * 32) % G::kCoutCta;
       const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
       float *patch = reinterpret_cast<float *>(smem + L::kVOff) + tw * L::kPatchFloats;
       const float bk = (bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
       const long long per_img = (long long)tiles_y * tiles_x;
       const int kmax = K - kq < 32 ? K - kq : 32;
 #pragma unroll 1
-      for (int gq = 0; gq < 2; ++gq) {
-        const int cb = col0 + gq * 16;
-        float z[4][16];
+      for (int gq = 0; gq < (kN / 4) / kE; ++gq) {
+        const int cb = col0 + gq * kE;
+        float z[TD][kE];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) tmem_ld16(trow + (uint32_t)(b * kPairTiles + cb), z[b]);
+        for (int b = 0; b < TD; ++b) {
+          if constexpr (kE == 16)
+            tmem_ld16(trow + (uint32_t)(b * kN + cb), z[b]);
+          else
+            tmem_ld8(trow + (uint32_t)(b * kN + cb), z[b]);
+        }
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          // Y[i][0] = Z0 + Z1 + Z2, Y[i][1] = Z1 - Z2 - Z3
-          float o0 = (z[0][j] + z[1][j]) + z[2][j] + bk;
-          float o1 = (z[1][j] - z[2][j]) - z[3][j] + bk;
-          if (relu) {
-            o0 = o0 < 0.f ? 0.f : o0;
-            o1 = o1 < 0.f ? 0.f : o1;
+        for (int e = 0; e < kE; ++e)
+#pragma unroll
+          for (int j = 0; j < M; ++j) {
+            // Y[i][j] = sum_b Z[i][b] At[j][b]
+            float s = 0.f;
+#pragma unroll
+            for (int b = 0; b < TD; ++b) {
+              const float cf = Wino<M>::at(j, b);
+              if (cf != 0.f) s = fmaf(cf, z[b][e], s);
+            }
+            s += bk;
+            if (relu) s = s < 0.f ? 0.f : s;
+            patch[lane * 33 + e * M + j] = s;
           }
-          patch[lane * 33 + 2 * j] = o0;
-          patch[lane * 33 + 2 * j + 1] = o1;
-        }
         __syncwarp();
-        const long long TT = pair0 + cb + (lane >> 1);
+        const long long TT = pair0 + cb + lane / M;
         if (TT < total_tiles && kmax > 0) {
           const int nn = (int)(TT / per_img);
           const int rem = (int)(TT - (long long)nn * per_img);
           const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
-          const int oy = 2 * yy + (int)rank, ox = 2 * xx + (lane & 1);
+          const int oy = M * yy + irow, ox = M * xx + lane % M;
           if (oy < H && ox < W) {
             Tio *dst = y + ((size_t)nn * K + kq) * plane + (size_t)oy * W + ox;
 #pragma unroll 4
@@ -1134,21 +1211,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Geo<true>::kThreads,
   }
 }
 
-template <bool X3, typename Tio>
+template <int M, bool X3, typename Tio>
 static cudaError_t launch_pair(const void *x, const void *U, const float *bias, void *y, int n,
                                int c, int k, int h, int w, int relu, cudaStream_t s) {
-  const int tiles_y = (h + 1) / 2, tiles_x = (w + 1) / 2;
+  using G = PairGeo<M>;
+  const int tiles_y = (h + M - 1) / M, tiles_x = (w + M - 1) / M;
   const long long total = (long long)n * tiles_y * tiles_x;
-  const long long pairs = (total + kPairTiles - 1) / kPairTiles;
-  const int gy = (k + kCout - 1) / kCout;
+  const long long pairs = (total + G::kN - 1) / G::kN;
+  const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
   if (2 * pairs > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidValue;
-  auto fn = wino_fused_tc_pair<X3, Tio>;
+  auto fn = wino_fused_tc_pair<M, X3, Tio>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       PairLayout<X3>::kSmem);
+                                       PairLayout<M, X3>::kSmem);
   if (e != cudaSuccess) return e;
-  fn<<<dim3((unsigned)(2 * pairs), (unsigned)gy), Geo<true>::kThreads, PairLayout<X3>::kSmem,
-       s>>>((const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y, tiles_x,
-            total, relu);
+  fn<<<dim3((unsigned)(2 * pairs), (unsigned)gy), G::kThreads, PairLayout<M, X3>::kSmem, s>>>(
+      (const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y, tiles_x, total,
+      relu);
   return cudaGetLastError();
 }
 
@@ -1159,19 +1237,31 @@ using namespace cwg;
 
 extern "C" {
 
-int cwgk_tc_get_cfg(int x3, int variant, cwgk_tc_cfg *out) {
+int cwgk_tc_get_cfg(int x3, int variant, int m, cwgk_tc_cfg *out) {
   if (!out) return -1;
-  out->m = 2;
+  out->m = m;
   out->kb = tc::kCout;
   out->cc = tc::kCc;
   out->tmem_cols = tc::kTmemCols;
+  if (variant == CWGK_TC_PAIR) {
+    if (m == 2) {
+      out->tiles = tc::PairGeo<2>::kN;
+      out->kb = tc::PairGeo<2>::kCoutCta;
+      out->threads = tc::PairGeo<2>::kThreads;
+      out->smem = x3 ? tc::PairLayout<2, true>::kSmem : tc::PairLayout<2, false>::kSmem;
+    } else if (m == 4) {
+      out->tiles = tc::PairGeo<4>::kN;
+      out->kb = tc::PairGeo<4>::kCoutCta;
+      out->threads = tc::PairGeo<4>::kThreads;
+      out->smem = x3 ? tc::PairLayout<4, true>::kSmem : tc::PairLayout<4, false>::kSmem;
+    } else {
+      return -1;
+    }
+    out->ctas_per_tile_block = 2;
+    return 0;
+  }
+  if (m != 2) return -1;
   switch (variant) {
-    case CWGK_TC_PAIR:
-      out->tiles = tc::kPairTiles;
-      out->threads = tc::Geo<true>::kThreads;
-      out->smem = x3 ? tc::PairLayout<true>::kSmem : tc::PairLayout<false>::kSmem;
-      out->ctas_per_tile_block = 2;
-      return 0;
     case CWGK_TC_HALF:
       out->tiles = tc::Geo<true>::kTiles;
       out->threads = tc::Geo<true>::kThreads;
@@ -1190,31 +1280,36 @@ int cwgk_tc_get_cfg(int x3, int variant, cwgk_tc_cfg *out) {
 
 int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int m, int layout,
                              int from_ref, void *stream) {
-  if (m != 2) return -2;
+  const bool pair = layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
+  const bool x3 = layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3;
+  if (!(m == 2 || (m == 4 && pair))) return -2;
+  if (!pair && layout != CWGK_LAYOUT_TC_X1 && layout != CWGK_LAYOUT_TC_X3) return -2;
+  const int kb = pair ? (m == 2 ? tc::PairGeo<2>::kCoutCta : tc::PairGeo<4>::kCoutCta) : tc::kCout;
   const int Cp = (c_in + tc::kCc - 1) / tc::kCc * tc::kCc;
-  const int Kp = (c_out + tc::kCout - 1) / tc::kCout * tc::kCout;
+  const int Kp = (c_out + kb - 1) / kb * kb;
   const long total = (long)Cp * Kp;
   const int threads = 256;
   const unsigned blocks = (unsigned)((total + threads - 1) / threads);
   cudaStream_t s = (cudaStream_t)stream;
   uint8_t *u = (uint8_t *)U;
-  switch (layout) {
-    case CWGK_LAYOUT_TC_X3:
-      tc::wt_transform_tc<true><<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref);
-      break;
-    case CWGK_LAYOUT_TC_X1:
-      tc::wt_transform_tc<false><<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref);
-      break;
-    case CWGK_LAYOUT_TC2_X3:
-      tc::wt_transform_tc_pair<true>
-          <<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref);
-      break;
-    case CWGK_LAYOUT_TC2_X1:
-      tc::wt_transform_tc_pair<false>
-          <<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref);
-      break;
-    default: return -2;
+#define CWG_WT(KERNEL) KERNEL<<<blocks, threads, 0, s>>>(src, u, c_in, c_out, Cp, Kp, from_ref)
+  if (!pair) {
+    if (x3)
+      CWG_WT(tc::wt_transform_tc<true>);
+    else
+      CWG_WT(tc::wt_transform_tc<false>);
+  } else if (m == 2) {
+    if (x3)
+      CWG_WT((tc::wt_transform_tc_pair<2, true>));
+    else
+      CWG_WT((tc::wt_transform_tc_pair<2, false>));
+  } else {
+    if (x3)
+      CWG_WT((tc::wt_transform_tc_pair<4, true>));
+    else
+      CWG_WT((tc::wt_transform_tc_pair<4, false>));
   }
+#undef CWG_WT
   cwgk_count_launch();
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
@@ -1225,21 +1320,27 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
 }
 
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
-                 int c_out, int h, int w, int x3, int variant, int bf16, int relu, void *stream) {
+                 int c_out, int h, int w, int m, int x3, int variant, int bf16, int relu,
+                 void *stream) {
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
 #define CWG_TC_LAUNCH(X3_, HALF_)                                                              \
   (bf16 ? tc::launch<X3_, HALF_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s) \
         : tc::launch<X3_, HALF_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
-#define CWG_TC_LAUNCH_PAIR(X3_)                                                                 \
-  (bf16 ? tc::launch_pair<X3_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s)    \
-        : tc::launch_pair<X3_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
-  switch (variant) {
-    case CWGK_TC_PAIR: e = x3 ? CWG_TC_LAUNCH_PAIR(true) : CWG_TC_LAUNCH_PAIR(false); break;
-    case CWGK_TC_HALF: e = x3 ? CWG_TC_LAUNCH(true, true) : CWG_TC_LAUNCH(false, true); break;
-    case CWGK_TC_FULL16: e = x3 ? CWG_TC_LAUNCH(true, false) : CWG_TC_LAUNCH(false, false); break;
-    default: return -2;
-  }
+#define CWG_TC_LAUNCH_PAIR(M_, X3_)                                                             \
+  (bf16 ? tc::launch_pair<M_, X3_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu,  \
+                                                   s)                                          \
+        : tc::launch_pair<M_, X3_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
+  if (variant == CWGK_TC_PAIR && m == 2)
+    e = x3 ? CWG_TC_LAUNCH_PAIR(2, true) : CWG_TC_LAUNCH_PAIR(2, false);
+  else if (variant == CWGK_TC_PAIR && m == 4)
+    e = x3 ? CWG_TC_LAUNCH_PAIR(4, true) : CWG_TC_LAUNCH_PAIR(4, false);
+  else if (variant == CWGK_TC_HALF && m == 2)
+    e = x3 ? CWG_TC_LAUNCH(true, true) : CWG_TC_LAUNCH(false, true);
+  else if (variant == CWGK_TC_FULL16 && m == 2)
+    e = x3 ? CWG_TC_LAUNCH(true, false) : CWG_TC_LAUNCH(false, false);
+  else
+    return -2;
 #undef CWG_TC_LAUNCH
 #undef CWG_TC_LAUNCH_PAIR
   cwgk_count_launch();

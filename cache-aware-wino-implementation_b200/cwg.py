@@ -48,6 +48,7 @@ class cwg_choice(ctypes.Structure):
         ("cout_per_cta", ctypes.c_int), ("cin_chunk", ctypes.c_int), ("threads", ctypes.c_int),
         ("smem_bytes", ctypes.c_int), ("tmem_cols", ctypes.c_int), ("ctas", ctypes.c_longlong),
         ("gemm_flops", ctypes.c_double), ("alg_bytes", ctypes.c_double),
+        ("mma_products", ctypes.c_int),
     ]
 
 
@@ -64,6 +65,7 @@ class Choice:
     ctas: int
     gemm_flops: float
     alg_bytes: float
+    mma_products: int
 
     @property
     def path_name(self) -> str:

@@ -74,6 +74,8 @@ typedef struct cwg_choice {
   long long ctas;    /* CTAs in the grid */
   double gemm_flops; /* 2 * tiles * C_out * C_in * (m+2)^2 */
   double alg_bytes;  /* x + y + U + bias, each touched once */
+  int mma_products;  /* bf16 tensor-core products per multiply-accumulate: 3 (hi/lo split,
+                        fp32-accurate) or 1; 0 on the FFMA path */
 } cwg_choice;
 
 /* ---- reference-compatible per-tile entry points (HOST pointers) ----------- */

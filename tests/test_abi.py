@@ -106,6 +106,29 @@ def test_selector_tensor_core_variants():
     assert e.value.status == cwg.EINVAL
 
 
+def test_selector_f43_tensor_core():
+    n, c, k, h, w = 2, 128, 200, 30, 30
+    tiles = n * 8 * 8  # 4x4 output tiles
+    ch = cwg.select(n, c, k, h, w, 4, cwg.BF16)
+    assert ch.path == cwg.PATH_TC and ch.m == 4 and ch.mma_products == 3
+    assert ch.tiles_per_cta == 64 and ch.cout_per_cta == 64
+    assert ch.ctas == 2 * (-(-tiles // 64)) * (-(-k // 64))
+    # weights: 36 frequencies x C_out padded to 64 x both rank sets x hi/lo
+    assert cwg.weight_bytes(c, k, 4, cwg.BF16) == 36 * 256 * 128 * 2 * 2 * 2
+    # bf16 F(2,3) runs single products; fp32 F(2,3) the hi/lo split
+    assert cwg.select(n, c, k, h, w, 0, cwg.BF16).mma_products == 1
+    assert cwg.select(n, c, k, h, w, 2).mma_products == 3
+    assert cwg.select(1, 32, 32, 8, 8, 4).mma_products == 0  # FFMA
+    # fp32 F(4,3) stays on the CUDA cores (tensor-core error above the fp32 bar)
+    assert cwg.select(n, c, k, h, w, 4).path == cwg.PATH_FFMA
+    # the single-CTA tensor-core kernels are F(2,3) only
+    assert cwg.select(n, c, k, h, w, 4, cwg.BF16 | cwg.TC_NOPAIR).path == cwg.PATH_FFMA
+    for fl in (cwg.FORCE_TC, cwg.BF16 | cwg.TC_NOPAIR | cwg.FORCE_TC):
+        with pytest.raises(cwg.CwgError) as e:
+            cwg.select(n, c, k, h, w, 4, fl)
+        assert e.value.status == cwg.EUNSUPPORTED
+
+
 def test_layer_call_argument_checks_need_no_gpu():
     L = cwg.lib()
     # NULL pointers / bad sizes are rejected before any CUDA call

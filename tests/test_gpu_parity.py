@@ -297,6 +297,23 @@ def test_tensor_core_variants_bf16(cuda_dev, variant):
     assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", f"bf16 {variant:#x}")
 
 
+F43_TC = [(2, 64, 64, 9, 13), (1, 96, 200, 7, 7), (3, 128, 64, 5, 22), (1, 64, 128, 24, 24)]
+
+
+@pytest.mark.parametrize("case", F43_TC, ids=lambda c: "x".join(map(str, c)))
+def test_tensor_core_f43_bf16(cuda_dev, case):
+    """F(4,3) on the pair kernel (6 accumulators, two output rows per CTA) for
+    bf16 layers: ragged tiles, partial channel blocks, tile blocks across
+    images."""
+    n, c, k, h, w = case
+    rng = np.random.default_rng(sum(case) + 500)
+    x = workloads.bf16_round(rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32))
+    g = workloads.bf16_round(rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32))
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    y = gpu_conv(x, g, bias, 4, cwg.BF16 | cwg.RELU | cwg.FORCE_TC, cuda_dev)
+    assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", f"bf16 {case}")
+
+
 def test_host_buffer_entry_matches_device_entry(cuda_dev):
     import torch
 
