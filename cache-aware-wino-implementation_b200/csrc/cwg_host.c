@@ -158,15 +158,16 @@ static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
     case CWGK_LAYOUT_TC_X1:
     case CWGK_LAYOUT_TC2_X3:
     case CWGK_LAYOUT_TC2_X1: {
+      /* [ceil(C_out / kb)][sets][C_pad / 16][nf][parts] blocks of 128 rows x 16
+       * channels (4096 bytes).  Pair layout: one set per rank, and a block's 128
+       * rows are m/2 output rows x kb = 128 / (m/2) channels. */
       const int pair = layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
-      /* output channels per weight block: 128 rows hold m/2 output rows of
-       * channels in the pair layout */
       const size_t kb = pair ? (size_t)(128 / (m / 2)) : 128;
-      const size_t kp = ((size_t)c_out + kb - 1) / kb * kb;
-      const size_t cp = ((size_t)c_in + 15) / 16 * 16;
+      const size_t nkb = ((size_t)c_out + kb - 1) / kb;
+      const size_t c16 = ((size_t)c_in + 15) / 16;
       const size_t parts = (layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3) ? 2 : 1;
       const size_t sets = pair ? 2 : 1;
-      return nf * kp * cp * 2 * parts * sets;
+      return nkb * sets * c16 * nf * parts * 4096;
     }
     default: return 0;
   }

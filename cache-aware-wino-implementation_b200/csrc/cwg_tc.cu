@@ -1083,12 +1083,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     } else {
       // group g takes the stages cs = g (mod 2), i.e. always V slot g.  Bt d Bt^T:
       // the row pass runs in place, then each output row a is formed, packed and
-      // stored, so two 6x6 windows fit the register budget.
+      // stored, so two 6x6 windows fit the register budget; once they are
+      // consumed, the group's next stage loads into the same registers.
+      if (grp < C16) load_stage(grp);
       for (int cs = grp; cs < C16; cs += G::kGroups) {
         const int vs = cs % kNV;
         ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
         if (!ok) break;
-        load_stage(cs);
         uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
 #pragma unroll
         for (int q = 0; q < 2; ++q)
@@ -1128,6 +1129,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(v_full + 8 * vs);
+        if (cs + G::kGroups < C16) load_stage(cs + G::kGroups);
       }
     }
 

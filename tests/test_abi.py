@@ -97,10 +97,11 @@ def test_selector_tensor_core_variants():
     single = cwg.select(n, c, k, h, w, 2, cwg.TC_NOPAIR)
     assert single.tiles_per_cta == 64 and single.ctas == (-(-tiles // 64)) * 2
     assert cwg.select(n, c, k, h, w, 2, cwg.TC_FULL16).tiles_per_cta == 32
-    # the pair layout holds both At-scaled row sets
+    # the pair layout holds both At-scaled row sets: [C_out/128][2][C_in/16][16 f][parts]
+    # blocks of 4096 bytes
     assert cwg.weight_bytes(c, k, 2) == 2 * cwg.weight_bytes(c, k, 2, cwg.TC_NOPAIR)
-    assert cwg.weight_bytes(c, k, 2, cwg.TC_NOPAIR) == 16 * 256 * 128 * 2 * 2
-    assert cwg.weight_bytes(c, k, 2, cwg.BF16) == 16 * 256 * 128 * 2 * 2
+    assert cwg.weight_bytes(c, k, 2, cwg.TC_NOPAIR) == 2 * 8 * 16 * 2 * 4096
+    assert cwg.weight_bytes(c, k, 2, cwg.BF16) == 2 * 2 * 8 * 16 * 1 * 4096
     with pytest.raises(cwg.CwgError) as e:
         cwg.select(n, c, k, h, w, 2, cwg.TC_NOPAIR | cwg.TC_FULL16)
     assert e.value.status == cwg.EINVAL
@@ -113,8 +114,9 @@ def test_selector_f43_tensor_core():
     assert ch.path == cwg.PATH_TC and ch.m == 4 and ch.mma_products == 3
     assert ch.tiles_per_cta == 64 and ch.cout_per_cta == 64
     assert ch.ctas == 2 * (-(-tiles // 64)) * (-(-k // 64))
-    # weights: 36 frequencies x C_out padded to 64 x both rank sets x hi/lo
-    assert cwg.weight_bytes(c, k, 4, cwg.BF16) == 36 * 256 * 128 * 2 * 2 * 2
+    # weights: [ceil(C_out/64)][2 ranks][C_in/16][36 f][hi, lo] blocks of 128 rows
+    # (2 output rows x 64 channels) x 16 channels x bf16
+    assert cwg.weight_bytes(c, k, 4, cwg.BF16) == 4 * 2 * 8 * 36 * 2 * 4096
     # bf16 F(2,3) runs single products; fp32 F(2,3) the hi/lo split
     assert cwg.select(n, c, k, h, w, 0, cwg.BF16).mma_products == 1
     assert cwg.select(n, c, k, h, w, 2).mma_products == 3

@@ -314,6 +314,27 @@ def test_tensor_core_f43_bf16(cuda_dev, case):
     assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", f"bf16 {case}")
 
 
+@pytest.mark.parametrize("case", [
+    (128, 200, 2, 0), (128, 200, 2, cwg.BF16), (128, 200, 2, cwg.TC_NOPAIR),
+    (128, 200, 2, cwg.TC_FULL16), (96, 200, 4, cwg.BF16), (32, 40, 2, 0), (32, 40, 4, cwg.BF16)],
+    ids=lambda c: f"c{c[0]}k{c[1]}m{c[2]}f{c[3]:#x}")
+def test_weight_transform_stays_in_its_buffer(cuda_dev, case):
+    """Every weight layout is written exactly inside cwg_weight_bytes: guard
+    bytes on both sides of the buffer keep their poison."""
+    import torch
+
+    c, k, m, flags = case
+    g = np.random.default_rng(7).normal(0, 0.1, (k, c, 3, 3)).astype(np.float32)
+    nb = cwg.weight_bytes(c, k, m, flags)
+    guard = 4096
+    buf = torch.full((nb + 2 * guard,), 0xA5, dtype=torch.uint8, device=cuda_dev)
+    U = buf[guard:guard + nb]
+    cwg.weight_transform(_t(g, cuda_dev), U, c, k, m, flags)
+    torch.cuda.synchronize()
+    assert bool((buf[:guard] == 0xA5).all()) and bool((buf[guard + nb:] == 0xA5).all())
+    assert not bool((U == 0xA5).all())
+
+
 def test_host_buffer_entry_matches_device_entry(cuda_dev):
     import torch
 
