@@ -766,15 +766,21 @@ struct PairGeo {
   static constexpr int kN = 2 * kTiles;             // MMA N of the pair
   static constexpr int kXWarps = 16;                // transform + epilogue warps
   static constexpr int kThreads = (2 + kXWarps) * 32;
-  // F(4,3): two groups of 8 warps transform alternate stages (a 6x6 window
-  // for two channels leaves no registers for a prefetched next stage).
+  // A thread transforms 2 channels of one tile.  F(2,3): all 16 warps take
+  // every stage, with the next stage's patches in registers meanwhile.
+  // F(4,3): two groups of 8 warps take alternate stages (two 6x6 windows fill
+  // the registers).  Splitting F(2,3) the same way, with 4 channels per thread
+  // and conflict-free 8-byte V stores, was slower (207 vs 190 us on a 64-image
+  // 128->128 56x56 layer): with two V slots each group's slot then stays busy
+  // through its own transform and the MMAs.
   static constexpr int kGroups = M == 2 ? 1 : 2;
   static constexpr int kGroupWarps = kXWarps / kGroups;
+  static constexpr int kCpt = 2;
   static constexpr int kNU = M == 2 ? 5 : 4;        // weight stages
   static constexpr int kVBytes = kTiles * kCc * 2;  // one frequency of V
   static constexpr int kEpiTiles = 32 / M;          // tiles per 32-pixel epilogue row
   static_assert(TD * kN <= kTmemCols, "accumulators fit TMEM");
-  static_assert(kTiles * 8 == kGroupWarps * 32, "one (tile, channel pair) per thread");
+  static_assert(kTiles * kCc == kGroupWarps * 32 * kCpt, "one (tile, channels) per thread");
 };
 
 // Pair weight layout: [ceil(C_out/cout_cta)][rank = 2][C_pad/16][NF f][parts][4096 B]:
@@ -1008,10 +1014,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     // ---------------- transform warps (this CTA's tiles), then epilogue ----------
     const int tw = warp - 2;
     const int grp = tw / G::kGroupWarps, gw = tw % G::kGroupWarps;
-    // warp -> (16-tile block, 4 channels); lane -> (tile, channel pair)
+    // warp -> (16-tile block, 2*CPT channels); lane -> (tile, CPT channels).  A
+    // warp load reads 16 consecutive tiles of 2 channel planes.
+    constexpr int CPT = G::kCpt;
     constexpr int kTileBlocks = kTiles / 16;
     const int cgrp = gw / kTileBlocks;
-    const int cbase = cgrp * 4 + (lane & 1) * 2;
+    const int cbase = cgrp * (2 * CPT) + (lane & 1) * CPT;
     const int kh = cbase >> 3;
     const int t = (gw % kTileBlocks) * 16 + (lane >> 1);
     const long long T = tile0 + t;
@@ -1033,10 +1041,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       rv[i] = tile_ok && (y0 + i) >= 0 && (y0 + i) < H;
       cv[i] = (x0 + i) >= 0 && (x0 + i) < W;
     }
-    float d[2][TD][TD];  // [channel][row][col]
+    float d[CPT][TD][TD];  // [channel][row][col]
     auto load_stage = [&](int cs) {
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
+      for (int q = 0; q < CPT; ++q) {
         const int c = cs * kCc + cbase + q;
         const bool cok = c < C;
         const Tio *xc = xn + (size_t)c * plane;
@@ -1049,62 +1057,73 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
                              : 0.f;
       }
     };
-    // V of frequency f, channels (cbase, cbase+1) of tile t: 4 bytes per part
-    auto put_v = [&](uint8_t *vb, int f, float e0, float e1) {
-      const uint32_t off = (uint32_t)(kh * (kTiles * 16) + t * 16 + (cbase & 7) * 2);
-      uint32_t hi, lo;
-      if (X3) {
-        split_pair(e0, e1, hi, lo);
-        *reinterpret_cast<uint32_t *>(vb + (NF + f) * kVBytes + off) = lo;
+    // V of frequency f, channels cbase .. cbase+CPT-1 of tile t: 2*CPT bytes per part
+    const uint32_t voff = (uint32_t)(kh * (kTiles * 16) + t * 16 + (cbase & 7) * 2);
+    auto put_v = [&](uint8_t *vb, int f, const float (&e)[CPT]) {
+      if constexpr (CPT == 4) {
+        uint2 hi, lo;
+        if (X3) {
+          split_pair(e[0], e[1], hi.x, lo.x);
+          split_pair(e[2], e[3], hi.y, lo.y);
+          *reinterpret_cast<uint2 *>(vb + (NF + f) * kVBytes + voff) = lo;
+        } else {
+          hi.x = pack_bf16(e[0], e[1]);
+          hi.y = pack_bf16(e[2], e[3]);
+        }
+        *reinterpret_cast<uint2 *>(vb + f * kVBytes + voff) = hi;
       } else {
-        hi = pack_bf16(e0, e1);
+        uint32_t hi, lo;
+        if (X3) {
+          split_pair(e[0], e[1], hi, lo);
+          *reinterpret_cast<uint32_t *>(vb + (NF + f) * kVBytes + voff) = lo;
+        } else {
+          hi = pack_bf16(e[0], e[1]);
+        }
+        *reinterpret_cast<uint32_t *>(vb + f * kVBytes + voff) = hi;
       }
-      *reinterpret_cast<uint32_t *>(vb + f * kVBytes + off) = hi;
     };
+    // Group g takes the stages cs = g (mod kGroups).  F(2,3): the next stage's
+    // patches load while this one is transformed and stored.  F(4,3): a
+    // stage's patches load before the wait for its V slot (the registers are
+    // free by then), overlapping the other group's stage and the MMAs.
     bool ok = true;
     if constexpr (M == 2) {
-      // every warp takes every stage; the next stage's patches load during this one
-      if (C16 > 0) load_stage(0);
-      for (int cs = 0; cs < C16; ++cs) {
-        const int vs = cs % kNV;
-        ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
-        if (!ok) break;
-        uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
-        float v[2][TD][TD];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) input_transform<M>(d[q], v[q]);
-#pragma unroll
-        for (int f = 0; f < NF; ++f) put_v(vb, f, v[0][f / TD][f % TD], v[1][f / TD][f % TD]);
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(v_full + 8 * vs);
-        if (cs + 1 < C16) load_stage(cs + 1);
-      }
-    } else {
-      // group g takes the stages cs = g (mod 2), i.e. always V slot g.  Bt d Bt^T:
-      // the row pass runs in place, then each output row a is formed, packed and
-      // stored, so two 6x6 windows fit the register budget; once they are
-      // consumed, the group's next stage loads into the same registers.
       if (grp < C16) load_stage(grp);
-      for (int cs = grp; cs < C16; cs += G::kGroups) {
-        const int vs = cs % kNV;
-        ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
-        if (!ok) break;
-        uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
+    }
+    for (int cs = grp; cs < C16; cs += G::kGroups) {
+      const int vs = cs % kNV;
+      if constexpr (M != 2) load_stage(cs);
+      ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
+      if (!ok) break;
+      uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
+      if constexpr (M == 2) {
+        float v[CPT][TD][TD];
 #pragma unroll
-        for (int q = 0; q < 2; ++q)
+        for (int q = 0; q < CPT; ++q) input_transform<M>(d[q], v[q]);
+#pragma unroll
+        for (int f = 0; f < NF; ++f) {
+          float e[CPT];
+#pragma unroll
+          for (int q = 0; q < CPT; ++q) e[q] = v[q][f / TD][f % TD];
+          put_v(vb, f, e);
+        }
+      } else {
+        // Bt d Bt^T: the row pass runs in place, then each output row a is
+        // formed, packed and stored, so two 6x6 windows fit the registers.
+#pragma unroll
+        for (int q = 0; q < CPT; ++q)
 #pragma unroll
           for (int i = 0; i < TD; ++i) {
             float w[TD];
 #pragma unroll
             for (int b = 0; b < TD; ++b) {
-              float s = 0.f;
+              float acc = 0.f;
 #pragma unroll
               for (int j = 0; j < TD; ++j) {
                 const float cf = Wino<M>::bt(b, j);
-                if (cf != 0.f) s = fmaf(cf, d[q][i][j], s);
+                if (cf != 0.f) acc = fmaf(cf, d[q][i][j], acc);
               }
-              w[b] = s;
+              w[b] = acc;
             }
 #pragma unroll
             for (int b = 0; b < TD; ++b) d[q][i][b] = w[b];
@@ -1113,22 +1132,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
         for (int a = 0; a < TD; ++a)
 #pragma unroll
           for (int b = 0; b < TD; ++b) {
-            float e[2];
+            float e[CPT];
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              float s = 0.f;
+            for (int q = 0; q < CPT; ++q) {
+              float acc = 0.f;
 #pragma unroll
               for (int i = 0; i < TD; ++i) {
                 const float cf = Wino<M>::bt(a, i);
-                if (cf != 0.f) s = fmaf(cf, d[q][i][b], s);
+                if (cf != 0.f) acc = fmaf(cf, d[q][i][b], acc);
               }
-              e[q] = s;
+              e[q] = acc;
             }
-            put_v(vb, a * TD + b, e[0], e[1]);
+            put_v(vb, a * TD + b, e);
           }
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(v_full + 8 * vs);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(v_full + 8 * vs);
+      if constexpr (M == 2) {
         if (cs + G::kGroups < C16) load_stage(cs + G::kGroups);
       }
     }
