@@ -212,6 +212,8 @@ def main() -> None:
     ap.add_argument("--flags", type=lambda s: int(s, 0), default=0,
                     help="extra CWG_* flags (ablations, e.g. 0x10 = FFMA path)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--n", type=int, default=0,
+                    help="images per GPU instead of the workload's own (small profiling cases)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -219,6 +221,8 @@ def main() -> None:
     rk = ranks.from_env()
     rank, world, local = rk.rank, rk.world, rk.local
     layer = workloads.config_layers(args.config)[args.layer]
+    if args.n > 0:
+        layer = layer.with_n(args.n)
 
     if args.impl == "reference":
         run_reference(args, layer, rank, world)
