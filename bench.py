@@ -14,6 +14,7 @@ host-buffer call (cwg_conv3x3_fused_host: H2D of x, kernel, D2H of y, sync).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config 1..5 --layer i]
   python bench.py --impl reference ...   # the reference's own CPU kernel
+  python bench.py --model resnet18|resnet34|vgg16 [--n N]   # chained stride-1 3x3 stack
 """
 from __future__ import annotations
 
@@ -198,6 +199,43 @@ def config_dict(layer, world: int, path: str, extra: dict | None = None) -> dict
     return d
 
 
+def run_model(args) -> None:
+    """The model's stride-1 3x3 convs (the shapes benchmarks/e2e_benchmark.py:91-137 of the
+    reference extracts) as one chained stack per step; per-layer and total device time."""
+    import torch
+
+    import cwg
+    import model_shapes
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n = args.n if args.n > 0 else 1
+    for _ in range(args.warmup):
+        model_shapes.run_stack(args.model, n, dev, args.flags)
+    torch.cuda.synchronize()
+    runs = [model_shapes.run_stack(args.model, n, dev, args.flags)[0] for _ in range(args.steps)]
+    per_layer = [statistics.median(r[i] for r in runs) for i in range(len(runs[0]))]
+    total_ms = sum(per_layer)
+    layers = model_shapes.stride1_layers(args.model)
+    flops = sum(2.0 * n * s.c_out * s.c_in * s.h * s.w * 9 for s in layers)
+    paths = [cwg.select(n, s.c_in, s.c_out, s.h, s.w, 0, args.flags | cwg.RELU).path_name
+             for s in layers]
+    print(json.dumps({
+        "metric": METRIC, "value": flops / (total_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms,
+        "us_per_layer": total_ms * 1e3 / len(layers), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if args.flags & cwg.BF16 else "f32",
+        "data": "synthetic (seeded U(-1,1) inputs, Kaiming-normal weights, bias U(-0.1,0.1))",
+        "config": {"workload": f"{args.model} stride-1 3x3 convs at 224x224 input, "
+                               f"{len(layers)} layers chained, N={n}, bias+ReLU",
+                   "layers": [{"c_in": s.c_in, "c_out": s.c_out, "hw": s.h, "path": p,
+                               "us": round(t * 1e3, 1)}
+                              for s, p, t in zip(layers, paths, per_layer)]},
+        "e2e": None,
+    }))
+
+
 # ---------------------------------------------------------------------------
 # GPU leg
 # ---------------------------------------------------------------------------
@@ -214,9 +252,14 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--n", type=int, default=0,
                     help="images per GPU instead of the workload's own (small profiling cases)")
+    ap.add_argument("--model", default="", choices=["", "resnet18", "resnet34", "vgg16"],
+                    help="time the model's stride-1 3x3 convs as a chained stack (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.model:
+        run_model(args)
+        return
 
     rk = ranks.from_env()
     rank, world, local = rk.rank, rk.world, rk.local

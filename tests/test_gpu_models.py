@@ -1,0 +1,23 @@
+"""Model shape feed on the GPU: every stride-1 3x3 conv of resnet18, resnet34 and vgg16 (at a
+224x224 input) runs as a chained stack through cwg_conv3x3_fused; each layer's output for
+image 0 is checked against the reference C on the exact input that layer received."""
+import pytest
+
+import model_shapes
+from conftest import assert_close
+from test_gpu_parity import oracle_conv
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("name", sorted(model_shapes.MODELS))
+def test_model_stack_matches_reference(cuda_dev, name):
+    layers = model_shapes.stride1_layers(name)
+    times, kept, prepared = model_shapes.run_stack(name, 2, cuda_dev, 0,
+                                                   keep=set(range(len(layers))))
+    assert len(times) == len(layers) and all(t > 0 for t in times)
+    assert len(kept) == len(layers)
+    for (i, s, x, y), (_, _, _, g, bias) in zip(kept, prepared):
+        xs = x[:1].float().cpu().numpy()
+        ys = y[:1].float().cpu().numpy()
+        assert_close(ys, oracle_conv(xs, g, bias, 2, True), "f23", f"{name} layer {i} {s}")
