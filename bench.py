@@ -252,6 +252,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--n", type=int, default=0,
                     help="images per GPU instead of the workload's own (small profiling cases)")
+    ap.add_argument("--nonfused", action="store_true",
+                    help="time the non-fused ablation (3 passes over HBM, fp32) instead")
     ap.add_argument("--model", default="", choices=["", "resnet18", "resnet34", "vgg16"],
                     help="time the model's stride-1 3x3 convs as a chained stack (1 GPU)")
     args = ap.parse_args()
@@ -281,6 +283,10 @@ def main() -> None:
 
     flags = (cwg.RELU if layer.relu else 0) | (cwg.BF16 if layer.bf16 else 0) | args.flags
     n, c, k, h, w, m = layer.n, layer.c_in, layer.c_out, layer.h, layer.w, layer.m
+    if args.nonfused:
+        if layer.bf16:
+            raise SystemExit("--nonfused: the ablation is fp32 only")
+        flags |= cwg.FORCE_FFMA  # U in the CUDA-core layout, which the ablation reads
     choice = cwg.select(n, c, k, h, w, m, flags)
     dt = torch.bfloat16 if layer.bf16 else torch.float32
     esz = 2 if layer.bf16 else 4
@@ -300,8 +306,17 @@ def main() -> None:
     ys = [torch.empty((n, k, h, w), dtype=dt, device=dev) for _ in range(nsets)]
     stream = torch.cuda.current_stream(dev)
 
-    def step(i):
-        cwg.conv3x3_fused(xs[i % nsets], U, b_d, ys[i % nsets], n, c, k, h, w, m, flags, stream)
+    if args.nonfused:
+        nf_b = cwg.nonfused_workspace_bytes(n, c, k, h, w, m)
+        nf_ws = torch.empty(nf_b, dtype=torch.uint8, device=dev)
+
+        def step(i):
+            cwg.conv3x3_nonfused(xs[i % nsets], U, b_d, ys[i % nsets], nf_ws, nf_b, n, c, k, h,
+                                 w, m, flags & cwg.RELU, stream)
+    else:
+        def step(i):
+            cwg.conv3x3_fused(xs[i % nsets], U, b_d, ys[i % nsets], n, c, k, h, w, m, flags,
+                              stream)
 
     for i in range(args.warmup):
         step(i)
@@ -326,28 +341,30 @@ def main() -> None:
     t_ms = ev0.elapsed_time(ev1) / args.steps
     t_max = ranks.max_over_ranks(t_ms, rk, dev)
 
-    # ---- end to end through the host-buffer entry point ----
-    xh = torch.from_numpy(x_host).to(dt).pin_memory() if layer.bf16 else \
-        torch.from_numpy(x_host).pin_memory()
-    yh = torch.empty((n, k, h, w), dtype=dt).pin_memory()
-    ws_b = cwg.host_workspace_bytes(n, c, k, h, w, flags)
-    ws = torch.empty(ws_b, dtype=torch.uint8, device=dev)
+    # ---- end to end through the host-buffer entry point (not for the ablation) ----
+    te_ms = None
+    if not args.nonfused:
+        xh = torch.from_numpy(x_host).to(dt).pin_memory() if layer.bf16 else \
+            torch.from_numpy(x_host).pin_memory()
+        yh = torch.empty((n, k, h, w), dtype=dt).pin_memory()
+        ws_b = cwg.host_workspace_bytes(n, c, k, h, w, flags)
+        ws = torch.empty(ws_b, dtype=torch.uint8, device=dev)
 
-    def e2e_step():
-        cwg.conv3x3_fused_host(int(xh.data_ptr()), U, b_d, int(yh.data_ptr()), ws, ws_b,
-                               n, c, k, h, w, m, flags, stream)
+        def e2e_step():
+            cwg.conv3x3_fused_host(int(xh.data_ptr()), U, b_d, int(yh.data_ptr()), ws, ws_b,
+                                   n, c, k, h, w, m, flags, stream)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    e2e_steps = max(3, min(args.steps, 20))
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    barrier()
-    te_ms = ranks.max_over_ranks(e0.elapsed_time(e1) / e2e_steps, rk, dev)
+        for _ in range(args.warmup):
+            e2e_step()
+        e2e_steps = max(3, min(args.steps, 20))
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        barrier()
+        te_ms = ranks.max_over_ranks(e0.elapsed_time(e1) / e2e_steps, rk, dev)
 
     # ---- verification checksum of every rank's output (outside timing) ----
     checksums = ranks.gather_floats(float(ys[0].double().sum().item()), rk, dev)
@@ -380,8 +397,11 @@ def main() -> None:
             "us_per_layer": t_max * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16" if layer.bf16 else "f32",
             "data": "synthetic (seeded U(-1,1) inputs, Kaiming-normal weights)",
-            "config": config_dict(layer, world, choice.path_name, {
-                "gemm": ("bf16x3 split (fp32 parity)" if products == 3 else
+            "config": config_dict(layer, world, "nonfused (input pass, cuBLAS SGEMM per "
+                                  "frequency, output pass)" if args.nonfused else
+                                  choice.path_name, {
+                "gemm": "fp32 cuBLAS SGEMM" if args.nonfused else
+                        ("bf16x3 split (fp32 parity)" if products == 3 else
                          ("bf16" if (flags & (cwg.BF16 | cwg.TC_SINGLE)) and
                           choice.path == cwg.PATH_TC else "fp32 FFMA")),
                 "l2": f"{nsets} rotating x/y buffer sets ({nsets * (xbytes + ybytes) / 2**20:.0f}"
@@ -389,9 +409,10 @@ def main() -> None:
                 "ctas": choice.ctas, "tiles_per_cta": choice.tiles_per_cta,
                 "cout_per_cta": choice.cout_per_cta}),
             "roofline": roof,
-            "e2e": {"value": flops_total / (te_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": xbytes, "d2h_bytes_per_step": ybytes,
-                    "us_per_layer": te_ms * 1e3},
+            "e2e": None if te_ms is None else {
+                "value": flops_total / (te_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": xbytes, "d2h_bytes_per_step": ybytes,
+                "us_per_layer": te_ms * 1e3},
             "gpu_launches": int(launches),
             "clocks": clk.summary(),
             "checksums": checksums,

@@ -31,6 +31,7 @@ EXPORTED = (
     "cwg_weight_transform", "cwg_weight_import", "cwg_conv3x3_fused",
     "cwg_host_workspace_bytes", "cwg_conv3x3_fused_host", "cwg_select", "cwg_strerror",
     "cwg_last_cuda_error", "cwg_device_status", "cwg_launch_count", "cwg_version",
+    "cwg_nonfused_workspace_bytes", "cwg_conv3x3_nonfused",
 )
 
 
@@ -117,6 +118,10 @@ def lib() -> ctypes.CDLL:
     L.cwg_launch_count.restype = ctypes.c_longlong
     L.cwg_version.argtypes = []
     L.cwg_version.restype = ctypes.c_char_p
+    L.cwg_nonfused_workspace_bytes.argtypes = [i, i, i, i, i, i]
+    L.cwg_nonfused_workspace_bytes.restype = sz
+    L.cwg_conv3x3_nonfused.argtypes = [vp, vp, vp, vp, vp, sz, i, i, i, i, i, i, u, vp]
+    L.cwg_conv3x3_nonfused.restype = i
     _lib = L
     return L
 
@@ -179,6 +184,19 @@ def conv3x3_fused(x, U, bias, y, n: int, c_in: int, c_out: int, h: int, w: int, 
                   flags: int = 0, stream=None) -> None:
     _check(lib().cwg_conv3x3_fused(_ptr(x), _ptr(U), _ptr(bias), _ptr(y), n, c_in, c_out, h, w,
                                    m, flags, _stream(stream)), "cwg_conv3x3_fused")
+
+
+def nonfused_workspace_bytes(n, c_in, c_out, h, w, m) -> int:
+    return int(lib().cwg_nonfused_workspace_bytes(n, c_in, c_out, h, w, m))
+
+
+def conv3x3_nonfused(x, U, bias, y, workspace, workspace_bytes: int, n: int, c_in: int,
+                     c_out: int, h: int, w: int, m: int, flags: int = 0, stream=None) -> None:
+    """Non-fused ablation: three passes over HBM (fp32; U from weight_transform with
+    FORCE_FFMA)."""
+    _check(lib().cwg_conv3x3_nonfused(_ptr(x), _ptr(U), _ptr(bias), _ptr(y), _ptr(workspace),
+                                      workspace_bytes, n, c_in, c_out, h, w, m, flags,
+                                      _stream(stream)), "cwg_conv3x3_nonfused")
 
 
 def host_workspace_bytes(n, c_in, c_out, h, w, flags=0) -> int:

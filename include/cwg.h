@@ -143,6 +143,22 @@ int cwg_conv3x3_fused_host_static(const void *x_host, const void *U, const float
                                   void *y_host, int n, int c_in, int c_out, int h, int w, int m,
                                   unsigned flags, void *stream);
 
+/* ---- non-fused ablation ---------------------------------------------------- */
+
+/* The same fp32 layer as three passes over HBM, for measuring what the fused
+ * kernels save: input transform -> V[(m+2)^2][c_in][T] in `workspace`, one
+ * cuBLAS SGEMM per frequency (FP32 math) -> M[(m+2)^2][c_out][T], output
+ * transform + bias (+ ReLU with CWG_RELU) -> y; T = n*ceil(h/m)*ceil(w/m).
+ * Mirrors the reference's run_non_fused (src/fused_winograd_kernel.py:116-151),
+ * whose math equals run_fused.  U in the CUDA-core layout: produce it with
+ * cwg_weight_transform(..., m, CWG_FORCE_FFMA, ...).  m = 2 or 4; fp32 only
+ * (any flag but CWG_RELU -> CWG_EINVAL); workspace 256-byte aligned, at least
+ * cwg_nonfused_workspace_bytes() bytes.  Device pointers; `stream` as above. */
+size_t cwg_nonfused_workspace_bytes(int n, int c_in, int c_out, int h, int w, int m);
+int cwg_conv3x3_nonfused(const float *x, const float *U, const float *bias, float *y,
+                         void *workspace, size_t workspace_bytes, int n, int c_in, int c_out,
+                         int h, int w, int m, unsigned flags, void *stream);
+
 /* ---- selector, diagnostics ----------------------------------------------- */
 
 /* Chooses m (when m == 0), the kernel path and its blocking for a layer on the

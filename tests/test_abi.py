@@ -131,6 +131,27 @@ def test_selector_f43_tensor_core():
         assert e.value.status == cwg.EUNSUPPORTED
 
 
+def test_nonfused_workspace_and_argument_checks():
+    # V[td^2][C][T] + M[td^2][K][T] fp32, each rounded up to 256 bytes
+    T = 2 * 28 * 28
+    assert cwg.nonfused_workspace_bytes(2, 32, 48, 56, 56, 2) == 16 * 32 * T * 4 + 16 * 48 * T * 4
+    T4 = 1 * 3 * 3
+    b = cwg.nonfused_workspace_bytes(1, 5, 7, 9, 10, 4)
+    assert b == -(-36 * 5 * T4 * 4 // 256) * 256 + -(-36 * 7 * T4 * 4 // 256) * 256
+    assert cwg.nonfused_workspace_bytes(1, 8, 8, 8, 8, 6) == 0
+    L = cwg.lib()
+    ws = cwg.nonfused_workspace_bytes(1, 8, 8, 8, 8, 2)
+    # bf16 / path flags, missing or short workspace: rejected before any CUDA call
+    assert L.cwg_conv3x3_nonfused(0x1000, 0x2000, None, 0x3000, 0x4000, ws, 1, 8, 8, 8, 8, 2,
+                                  cwg.BF16, None) == cwg.EINVAL
+    assert L.cwg_conv3x3_nonfused(0x1000, 0x2000, None, 0x3000, None, ws, 1, 8, 8, 8, 8, 2, 0,
+                                  None) == cwg.EINVAL
+    assert L.cwg_conv3x3_nonfused(0x1000, 0x2000, None, 0x3000, 0x4000, ws - 1, 1, 8, 8, 8, 8, 2,
+                                  0, None) == cwg.EINVAL
+    assert L.cwg_conv3x3_nonfused(0x1000, 0x2000, None, 0x3000, 0x4000, ws, 1, 8, 8, 8, 8, 6, 0,
+                                  None) == cwg.EUNSUPPORTED
+
+
 def test_layer_call_argument_checks_need_no_gpu():
     L = cwg.lib()
     # NULL pointers / bad sizes are rejected before any CUDA call

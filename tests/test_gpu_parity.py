@@ -335,6 +335,30 @@ def test_weight_transform_stays_in_its_buffer(cuda_dev, case):
     assert not bool((U == 0xA5).all())
 
 
+@pytest.mark.parametrize("case", [(2, 32, 48, 15, 17, 2), (1, 128, 128, 56, 56, 2),
+                                  (1, 64, 64, 21, 19, 4), (2, 16, 32, 9, 9, 4)],
+                         ids=lambda c: "x".join(map(str, c)))
+def test_nonfused_ablation_matches_reference(cuda_dev, case):
+    """The three-pass ablation (input transform -> HBM -> cuBLAS SGEMM per frequency ->
+    output transform) computes the same layer."""
+    import torch
+
+    n, c, k, h, w, m = case
+    rng = np.random.default_rng(sum(case) + 600)
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    U = make_U(g, c, k, m, cwg.FORCE_FFMA, cuda_dev)
+    ws_b = cwg.nonfused_workspace_bytes(n, c, k, h, w, m)
+    ws = torch.empty(ws_b, dtype=torch.uint8, device=cuda_dev)
+    y = torch.full((n, k, h, w), float("nan"), device=cuda_dev)
+    cwg.conv3x3_nonfused(_t(x, cuda_dev), U, _t(bias, cuda_dev), y, ws, ws_b, n, c, k, h, w, m,
+                         cwg.RELU)
+    cwg.device_status()
+    ref = oracle_conv(x, g, bias, m, True)
+    assert_close(y.cpu().numpy(), ref, "f23" if m == 2 else "f43", str(case))
+
+
 def test_host_buffer_entry_matches_device_entry(cuda_dev):
     import torch
 
