@@ -10,8 +10,8 @@
 namespace cwg {
 
 // ---- weight transform G g G^T ------------------------------------------------
-// G for F(2,3) and F(4,3): the unique matrices that make the reference's Bt/At
-// (src/fused_winograd_kernel.py:18-46) compute a 3x3 cross-correlation.
+// G for F(2,3), F(4,3) and F(6,3): the unique matrices that make the reference's Bt/At
+// (src/fused_winograd_kernel.py:18-67) compute a 3x3 cross-correlation.
 template <int M>
 __device__ __forceinline__ double gmat(int a, int i);
 template <>
@@ -24,6 +24,19 @@ __device__ __forceinline__ double gmat<4>(int a, int i) {
   const double g[6][3] = {{1. / 4, 0, 0},          {-1. / 6, -1. / 6, -1. / 6},
                           {-1. / 6, 1. / 6, -1. / 6}, {1. / 24, 1. / 12, 1. / 6},
                           {1. / 24, -1. / 12, 1. / 6}, {0, 0, 1}};
+  return g[a][i];
+}
+
+template <>
+__device__ __forceinline__ double gmat<6>(int a, int i) {
+  const double g[8][3] = {{1, 0, 0},
+                          {-2. / 9, -2. / 9, -2. / 9},
+                          {-2. / 9, 2. / 9, -2. / 9},
+                          {1. / 90, 1. / 45, 2. / 45},
+                          {1. / 90, -1. / 45, 2. / 45},
+                          {1. / 45, 1. / 90, 1. / 180},
+                          {1. / 45, -1. / 90, 1. / 180},
+                          {0, 0, 1}};
   return g[a][i];
 }
 

@@ -145,8 +145,14 @@ __device__ __forceinline__ void v_row_dispatch(int a, const float (&d)[M + 2][M 
     case 3: v_row<M, 3>(d, out); break;
     default:
       if constexpr (M + 2 > 4) {
-        if (a == 4) v_row<M, 4>(d, out);
-        else v_row<M, 5>(d, out);
+        if (a == 4) {
+          v_row<M, 4>(d, out);
+        } else if (a == 5) {
+          v_row<M, 5>(d, out);
+        } else if constexpr (M + 2 > 6) {
+          if (a == 6) v_row<M, 6>(d, out);
+          else v_row<M, 7>(d, out);
+        }
       }
   }
 }
@@ -416,6 +422,9 @@ static const FfmaEntry kFfma[] = {
     CWG_FFMA_ENTRY(2, 4, 4, 64, 8, 1), CWG_FFMA_ENTRY(2, 8, 8, 32, 8, 1),
     CWG_FFMA_ENTRY(4, 4, 4, 16, 8, 3), CWG_FFMA_ENTRY(4, 4, 4, 32, 8, 3),
     CWG_FFMA_ENTRY(4, 4, 4, 64, 8, 3),
+    // F(6,3): a 32-channel block spills ~290 B per thread (64 accumulators beside
+    // the 8x8 window rows); the 16-channel block keeps it to ~80 B.
+    CWG_FFMA_ENTRY(6, 4, 4, 16, 8, 4),
 };
 constexpr int kNumFfma = sizeof(kFfma) / sizeof(kFfma[0]);
 
@@ -455,6 +464,8 @@ int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m,
     wt_transform_ffma<2><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out, from_ref);
   else if (m == 4)
     wt_transform_ffma<4><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out, from_ref);
+  else if (m == 6)
+    wt_transform_ffma<6><<<blocks, threads, 0, s>>>(src, (float *)U, c_in, c_out, from_ref);
   else
     return -2;
   cwgk_count_launch();

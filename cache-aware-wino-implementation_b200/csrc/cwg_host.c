@@ -113,7 +113,7 @@ static int tc_shape_ok(int c_in, int c_out) { return c_in >= 64 && c_out >= 64; 
 /* Resolves m and the path; returns CWG_OK or an error. */
 static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *path_out) {
   if (c_in <= 0 || c_out <= 0) return CWG_EINVAL;
-  if (m != 0 && m != 2 && m != 4) return (m == 6) ? CWG_EUNSUPPORTED : CWG_EINVAL;
+  if (m != 0 && m != 2 && m != 4 && m != 6) return CWG_EINVAL;
   if ((flags & CWG_FORCE_FFMA) && (flags & CWG_FORCE_TC)) return CWG_EINVAL;
   if ((flags & CWG_TC_FULL16) && (flags & CWG_TC_NOPAIR)) return CWG_EINVAL;
   /* the tensor-core path runs F(2,3) unless F(4,3) is asked for */
@@ -189,7 +189,11 @@ static int pick_ffma(int n, int c_out, int h, int w, int m, cwgk_ffma_cfg *cfg_o
   for (;;) {
     cwgk_ffma_cfg c;
     const int idx = find_ffma(m, kb, &c);
-    if (idx < 0) return -1;
+    if (idx < 0) {  /* no kernel with this channel block for this m: try a smaller one */
+      if (kb == 16) return -1;
+      kb /= 2;
+      continue;
+    }
     const long long ctas = (long long)n * ((th + c.ty - 1) / c.ty) * ((tw + c.tx - 1) / c.tx) *
                            ((c_out + c.kb - 1) / c.kb);
     if (ctas >= sms || kb == 16) {

@@ -106,7 +106,8 @@ using namespace cwg;
 static size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 
 extern "C" size_t cwg_nonfused_workspace_bytes(int n, int c_in, int c_out, int h, int w, int m) {
-  if (n <= 0 || c_in <= 0 || c_out <= 0 || h <= 0 || w <= 0 || (m != 2 && m != 4)) return 0;
+  if (n <= 0 || c_in <= 0 || c_out <= 0 || h <= 0 || w <= 0 || (m != 2 && m != 4 && m != 6))
+    return 0;
   const size_t T = (size_t)n * ((h + m - 1) / m) * ((w + m - 1) / m);
   const size_t nf = (size_t)(m + 2) * (m + 2);
   return al256(nf * c_in * T * 4) + al256(nf * c_out * T * 4);
@@ -118,7 +119,7 @@ extern "C" int cwg_conv3x3_nonfused(const float *x, const float *U, const float 
                                     void *stream) {
   if (flags & ~(unsigned)CWG_RELU) return CWG_EINVAL;  // fp32 only, no path switches
   const size_t need = cwg_nonfused_workspace_bytes(n, c_in, c_out, h, w, m);
-  if (need == 0) return (m == 6) ? CWG_EUNSUPPORTED : CWG_EINVAL;
+  if (need == 0) return CWG_EINVAL;
   if (!x || !U || !y || !workspace || workspace_bytes < need) return CWG_EINVAL;
   if (((uintptr_t)x & 3) || ((uintptr_t)y & 3) || ((uintptr_t)U & 3) || ((uintptr_t)bias & 3) ||
       ((uintptr_t)workspace & 255))
@@ -143,8 +144,10 @@ extern "C" int cwg_conv3x3_nonfused(const float *x, const float *U, const float 
   const unsigned bx = (unsigned)(((long long)c_in * T + threads - 1) / threads);
   if (m == 2)
     nonfused::input_pass<2><<<bx, threads, 0, s>>>(x, V, c_in, h, w, tiles_y, tiles_x, T);
-  else
+  else if (m == 4)
     nonfused::input_pass<4><<<bx, threads, 0, s>>>(x, V, c_in, h, w, tiles_y, tiles_x, T);
+  else
+    nonfused::input_pass<6><<<bx, threads, 0, s>>>(x, V, c_in, h, w, tiles_y, tiles_x, T);
   cwgk_count_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) {
     cwgk_set_cuda_error((int)e);
@@ -164,8 +167,11 @@ extern "C" int cwg_conv3x3_nonfused(const float *x, const float *U, const float 
   if (m == 2)
     nonfused::output_pass<2>
         <<<by, threads, 0, s>>>(Mf, bias, y, c_out, h, w, tiles_y, tiles_x, T, relu);
-  else
+  else if (m == 4)
     nonfused::output_pass<4>
+        <<<by, threads, 0, s>>>(Mf, bias, y, c_out, h, w, tiles_y, tiles_x, T, relu);
+  else
+    nonfused::output_pass<6>
         <<<by, threads, 0, s>>>(Mf, bias, y, c_out, h, w, tiles_y, tiles_x, T, relu);
   cwgk_count_launch();
   if ((e = cudaGetLastError()) != cudaSuccess) {

@@ -63,7 +63,8 @@ extern "C" {
 
 /* Result of the tile selector.  All fields are outputs. */
 typedef struct cwg_choice {
-  int m;             /* output tile edge: 2 -> F(2x2,3x3), 4 -> F(4x4,3x3) */
+  int m;             /* output tile edge: 2 -> F(2x2,3x3), 4 -> F(4x4,3x3), 6 -> F(6x6,3x3)
+                        (CUDA-core path only) */
   int path;          /* CWG_PATH_* */
   int tiles_per_cta; /* output tiles one CTA owns (one CTA pair, for the 2-SM kernel) */
   int cout_per_cta;  /* output channels one CTA owns */
@@ -151,7 +152,7 @@ int cwg_conv3x3_fused_host_static(const void *x_host, const void *U, const float
  * transform + bias (+ ReLU with CWG_RELU) -> y; T = n*ceil(h/m)*ceil(w/m).
  * Mirrors the reference's run_non_fused (src/fused_winograd_kernel.py:116-151),
  * whose math equals run_fused.  U in the CUDA-core layout: produce it with
- * cwg_weight_transform(..., m, CWG_FORCE_FFMA, ...).  m = 2 or 4; fp32 only
+ * cwg_weight_transform(..., m, CWG_FORCE_FFMA, ...).  m = 2, 4 or 6; fp32 only
  * (any flag but CWG_RELU -> CWG_EINVAL); workspace 256-byte aligned, at least
  * cwg_nonfused_workspace_bytes() bytes.  Device pointers; `stream` as above. */
 size_t cwg_nonfused_workspace_bytes(int n, int c_in, int c_out, int h, int w, int m);

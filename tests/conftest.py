@@ -26,6 +26,7 @@ def load_golden(name):
 TOL = {
     "f23": (1e-4, 1e-3),   # fp32 F(2x2,3x3) vs the reference C
     "f43": (1e-4, 5e-3),   # fp32 F(4x4,3x3) vs the C restatement of run_fused
+    "f63": (1e-3, 5e-3),   # fp32 F(6x6,3x3) vs the C restatement (transform entries up to 32)
     "bf16": (None, 1e-2),  # bf16 I/O vs fp64 direct conv on bf16-rounded x, g
 }
 

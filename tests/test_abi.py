@@ -72,7 +72,8 @@ def test_selector_grid_covers_layer():
     ((1, 32, 0, 56, 56, 2, 0), cwg.EINVAL),
     ((1, 32, 32, 0, 56, 2, 0), cwg.EINVAL),
     ((1, 32, 32, 56, 56, 3, 0), cwg.EINVAL),
-    ((1, 32, 32, 56, 56, 6, 0), cwg.EUNSUPPORTED),
+    ((1, 32, 32, 56, 56, 8, 0), cwg.EINVAL),
+    ((1, 128, 128, 56, 56, 6, cwg.FORCE_TC), cwg.EUNSUPPORTED),
     ((1, 32, 32, 56, 56, 2, cwg.FORCE_FFMA | cwg.FORCE_TC), cwg.EINVAL),
 ])
 def test_selector_rejects(args, status):
@@ -85,7 +86,15 @@ def test_weight_bytes():
     assert cwg.weight_bytes(32, 32, 2, cwg.FORCE_FFMA) == 16 * 32 * 32 * 4
     assert cwg.weight_bytes(32, 32, 4, cwg.FORCE_FFMA | cwg.BF16) == 36 * 32 * 32 * 4
     assert cwg.weight_bytes(0, 32, 2) == 0
-    assert cwg.weight_bytes(32, 32, 6) == 0
+    assert cwg.weight_bytes(32, 32, 6) == 64 * 32 * 32 * 4  # F(6,3): CUDA cores, fp32 U
+    assert cwg.weight_bytes(32, 32, 8) == 0
+
+
+def test_selector_f63_runs_on_cuda_cores():
+    ch = cwg.select(2, 128, 128, 60, 60, 6)
+    assert ch.path == cwg.PATH_FFMA and ch.m == 6 and ch.mma_products == 0
+    assert ch.tiles_per_cta == 16 and ch.cout_per_cta == 16
+    assert ch.ctas == 2 * 3 * 3 * 8  # 10x10 tiles of 6x6 -> 3x3 blocks of 4x4 tiles
 
 
 def test_selector_tensor_core_variants():
@@ -138,7 +147,8 @@ def test_nonfused_workspace_and_argument_checks():
     T4 = 1 * 3 * 3
     b = cwg.nonfused_workspace_bytes(1, 5, 7, 9, 10, 4)
     assert b == -(-36 * 5 * T4 * 4 // 256) * 256 + -(-36 * 7 * T4 * 4 // 256) * 256
-    assert cwg.nonfused_workspace_bytes(1, 8, 8, 8, 8, 6) == 0
+    assert cwg.nonfused_workspace_bytes(1, 8, 8, 8, 8, 8) == 0
+    assert cwg.nonfused_workspace_bytes(1, 8, 8, 12, 12, 6) == 2 * (64 * 8 * 4 * 4)
     L = cwg.lib()
     ws = cwg.nonfused_workspace_bytes(1, 8, 8, 8, 8, 2)
     # bf16 / path flags, missing or short workspace: rejected before any CUDA call
@@ -148,8 +158,8 @@ def test_nonfused_workspace_and_argument_checks():
                                   None) == cwg.EINVAL
     assert L.cwg_conv3x3_nonfused(0x1000, 0x2000, None, 0x3000, 0x4000, ws - 1, 1, 8, 8, 8, 8, 2,
                                   0, None) == cwg.EINVAL
-    assert L.cwg_conv3x3_nonfused(0x1000, 0x2000, None, 0x3000, 0x4000, ws, 1, 8, 8, 8, 8, 6, 0,
-                                  None) == cwg.EUNSUPPORTED
+    assert L.cwg_conv3x3_nonfused(0x1000, 0x2000, None, 0x3000, 0x4000, ws, 1, 8, 8, 8, 8, 8, 0,
+                                  None) == cwg.EINVAL
 
 
 def test_layer_call_argument_checks_need_no_gpu():

@@ -56,7 +56,7 @@ def gpu_conv(x, g, bias, m, flags, dev, U_ref=None, U=None):
 
 
 def oracle_conv(x, g, bias, m, relu):
-    """Reference C for F(2,3) (when built), C restatement for F(4,3)."""
+    """Reference C for F(2,3) (when built), C restatement for F(4,3) and F(6,3)."""
     td = m + 2
     U = oracle.weight_transform(g, td)
     if m == 2 and oracle.ref_available():
@@ -129,10 +129,28 @@ def test_layer_goldens(cuda_dev, name, how):
     assert_close(y, z["y"], "f23" if m == 2 else "f43", name)
 
 
-def test_layer_f63_is_unsupported(cuda_dev):
-    with pytest.raises(cwg.CwgError) as e:
-        cwg.weight_bytes(8, 8, 6) or cwg.select(1, 8, 8, 8, 8, 6)
-    assert e.value.status == cwg.EUNSUPPORTED
+@pytest.mark.parametrize("case", [(1, 8, 8, 12, 12), (2, 21, 35, 17, 23), (1, 128, 128, 60, 60),
+                                  (1, 64, 64, 7, 7)], ids=lambda c: "x".join(map(str, c)))
+def test_layer_f63(cuda_dev, case):
+    """F(6x6,3x3) on the CUDA-core kernel against the C restatement of run_fused
+    (td = 8, the reference's _BT_8/_AT_8)."""
+    n, c, k, h, w = case
+    rng = np.random.default_rng(sum(case) + 700)
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    y = gpu_conv(x, g, bias, 6, cwg.RELU, cuda_dev)
+    U = oracle.weight_transform(g, 8)
+    assert_close(y, oracle.conv_layer(x, U, bias, 8, True), "f63", str(case))
+
+
+def test_layer_f63_bf16(cuda_dev):
+    rng = np.random.default_rng(701)
+    x = workloads.bf16_round(rng.uniform(-1, 1, (2, 64, 30, 30)).astype(np.float32))
+    g = workloads.bf16_round(rng.normal(0, np.sqrt(2 / 576), (48, 64, 3, 3)).astype(np.float32))
+    bias = rng.uniform(-0.1, 0.1, 48).astype(np.float32)
+    y = gpu_conv(x, g, bias, 6, cwg.BF16 | cwg.RELU, cuda_dev)
+    assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", "bf16 F(6,3)")
 
 
 # ---- the benchmark configurations -----------------------------------------------
@@ -336,7 +354,8 @@ def test_weight_transform_stays_in_its_buffer(cuda_dev, case):
 
 
 @pytest.mark.parametrize("case", [(2, 32, 48, 15, 17, 2), (1, 128, 128, 56, 56, 2),
-                                  (1, 64, 64, 21, 19, 4), (2, 16, 32, 9, 9, 4)],
+                                  (1, 64, 64, 21, 19, 4), (2, 16, 32, 9, 9, 4),
+                                  (1, 32, 40, 20, 26, 6)],
                          ids=lambda c: "x".join(map(str, c)))
 def test_nonfused_ablation_matches_reference(cuda_dev, case):
     """The three-pass ablation (input transform -> HBM -> cuBLAS SGEMM per frequency ->
@@ -356,7 +375,7 @@ def test_nonfused_ablation_matches_reference(cuda_dev, case):
                          cwg.RELU)
     cwg.device_status()
     ref = oracle_conv(x, g, bias, m, True)
-    assert_close(y.cpu().numpy(), ref, "f23" if m == 2 else "f43", str(case))
+    assert_close(y.cpu().numpy(), ref, {2: "f23", 4: "f43", 6: "f63"}[m], str(case))
 
 
 def test_host_buffer_entry_matches_device_entry(cuda_dev):
@@ -393,7 +412,11 @@ def test_errors_and_launch_counter(cuda_dev):
     with pytest.raises(cwg.CwgError) as e:  # misaligned output pointer
         cwg.conv3x3_fused(x_d, U, None, int(y_d.data_ptr()) + 2, 1, 8, 8, 8, 8, 2, 0)
     assert e.value.status == cwg.EINVAL
-    with pytest.raises(cwg.CwgError) as e:
-        cwg.conv3x3_fused(x_d, U, None, y_d, 1, 8, 8, 8, 8, 6, 0)
+    # rejected on the host, before any launch
+    with pytest.raises(cwg.CwgError) as e:  # no F(8x8,3x3)
+        cwg.conv3x3_fused(x_d, U, None, y_d, 1, 8, 8, 8, 8, 8, 0)
+    assert e.value.status == cwg.EINVAL
+    with pytest.raises(cwg.CwgError) as e:  # F(6,3) has no tensor-core kernel
+        cwg.conv3x3_fused(x_d, U, None, y_d, 1, 8, 8, 8, 8, 6, cwg.FORCE_TC)
     assert e.value.status == cwg.EUNSUPPORTED
     cwg.device_status()
