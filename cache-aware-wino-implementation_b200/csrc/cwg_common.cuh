@@ -5,9 +5,32 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "cwg_internal.h"
 
 namespace cwg {
+
+// ---- launch bookkeeping ---------------------------------------------------------
+// The opt-in shared-memory size of a kernel, set once per (kernel, device): later
+// launches skip the call, so per-layer host cost stays low and a stream capture
+// into a CUDA graph sees launches only.  `done` holds one bit per device.
+inline cudaError_t smem_attr_once(std::atomic<unsigned long long> &done, const void *fn,
+                                  int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = dev < 64 ? 1ull << dev : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
+  return e;
+}
+template <auto Kernel>
+inline cudaError_t smem_attr_once(int bytes) {
+  static std::atomic<unsigned long long> done{0};
+  return smem_attr_once(done, (const void *)Kernel, bytes);
+}
 
 // ---- weight transform G g G^T ------------------------------------------------
 // G for F(2,3), F(4,3) and F(6,3): the unique matrices that make the reference's Bt/At

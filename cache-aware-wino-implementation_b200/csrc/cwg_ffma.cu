@@ -484,8 +484,8 @@ int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias,
   const unsigned gy = (unsigned)((c_out + e.cfg.kb - 1) / e.cfg.kb);
   if (n > 65535 || gy > 65535) return -2;
   const void *fn = bf16 ? e.fn_bf16 : e.fn_f32;
-  cudaError_t err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         e.cfg.smem);
+  static std::atomic<unsigned long long> attr_done[kNumFfma][2];
+  cudaError_t err = smem_attr_once(attr_done[cfg_idx][bf16 ? 1 : 0], fn, e.cfg.smem);
   if (err != cudaSuccess) return fail(err);
   void *args[] = {(void *)&x,  (void *)&U, (void *)&bias,    (void *)&y,       (void *)&c_in,
                   (void *)&c_out, (void *)&h, (void *)&w, (void *)&tiles_y, (void *)&tiles_x,

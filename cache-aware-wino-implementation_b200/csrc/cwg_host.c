@@ -231,7 +231,9 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
     out->smem_bytes = t.smem;
     out->tmem_cols = t.tmem_cols;
     out->ctas = ((long long)n * th * tw + t.tiles - 1) / t.tiles * ((c_out + t.kb - 1) / t.kb) *
-                t.ctas_per_tile_block;
+                t.ctas_per_tile_block *
+                cwgk_tc_splits(n, c_in, c_out, h, w, mm, tc_variant(flags),
+                               (flags & CWG_BF16) != 0, !(flags & CWG_NO_SPLIT), num_sms());
   } else {
     cwgk_ffma_cfg c;
     if (pick_ffma(n, c_out, h, w, mm, &c) < 0) return CWG_EUNSUPPORTED;
@@ -293,7 +295,7 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   const int bf16 = (flags & CWG_BF16) ? 1 : 0;
   if (path == CWG_PATH_TC) {
     return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, mm, tc_x3(mm, flags),
-                        tc_variant(flags), bf16, relu, stream);
+                        tc_variant(flags), bf16, relu, !(flags & CWG_NO_SPLIT), stream);
   }
   cwgk_ffma_cfg cfg;
   const int idx = pick_ffma(n, c_out, h, w, mm, &cfg);

@@ -68,10 +68,16 @@ int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias,
 
 /* tcgen05 fused convolution F(m x m, 3x3) (C_in padded to 16 and C_out to the
  * channel block by the weight layout), kernel `variant` (CWGK_TC_*; the
- * single-CTA variants are F(2,3) only). */
+ * single-CTA variants are F(2,3) only).  allow_split: the pair kernel may split
+ * the C_in reduction of small fp32 layers across CTAs (y zeroed, partial sums
+ * added atomically, bias and ReLU in a second pass). */
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
                  int c_out, int h, int w, int m, int x3, int variant, int bf16, int relu,
-                 void *stream);
+                 int allow_split, void *stream);
+
+/* C_in slices the tensor-core path uses for this layer (1 = no split). */
+int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant, int bf16,
+                   int allow_split, int sms);
 
 /* Per-tile kernel on device buffers (reference layouts). */
 int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,

@@ -655,8 +655,7 @@ static cudaError_t launch(const void *x, const void *U, const float *bias, void 
   const int gy = (k + kCout - 1) / kCout;
   if (gx > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidValue;
   auto fn = wino_fused_tc<X3, HALF, Tio>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       Layout<X3, HALF>::kSmem);
+  cudaError_t e = smem_attr_once<wino_fused_tc<X3, HALF, Tio>>(Layout<X3, HALF>::kSmem);
   if (e != cudaSuccess) return e;
   fn<<<dim3((unsigned)gx, (unsigned)gy), Geo<HALF>::kThreads, Layout<X3, HALF>::kSmem, s>>>(
       (const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y, tiles_x, total,
@@ -853,7 +852,8 @@ template <int M, bool X3, typename Tio>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads, 1)
     wino_fused_tc_pair(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                        const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
-                       int W, int tiles_y, int tiles_x, long long total_tiles, int relu) {
+                       int W, int tiles_y, int tiles_x, long long total_tiles, int relu,
+                       int cs_per_split, int split) {
   using L = PairLayout<M, X3>;
   using G = PairGeo<M>;
   constexpr int P = L::kParts, TD = G::TD, NF = G::NF;
@@ -875,6 +875,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();  // 0: issues the MMAs
   const int C16 = (C + kCc - 1) / kCc;
+  // this CTA's slice of the C_in reduction (blockIdx.z; one slice unless split)
+  const int cs0 = (int)blockIdx.z * cs_per_split;
+  const int nst = C16 - cs0 < cs_per_split ? C16 - cs0 : cs_per_split;
   const int kblk = blockIdx.y;
   const long long pair0 = (long long)(blockIdx.x >> 1) * kN;  // first tile of the pair
   const long long tile0 = pair0 + (long long)rank * kTiles;  // this CTA's V columns
@@ -916,7 +919,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       const uint64_t b0 = smem_desc(sbase + L::kVOff, (uint32_t)(kTiles * 16), 128);
       bool ok = true;
       int ui = 0;
-      for (int cs = 0; cs < C16; ++cs) {
+      for (int cs = 0; cs < nst; ++cs) {
         const int vs = cs % kNV;
         ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort) &&
                                          mbar_wait(v_peer + 8 * vs, (cs / kNV) & 1, abort));
@@ -972,7 +975,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       const uint32_t v_peer_r0 = mapa_shared(v_peer, 0), u_peer_r0 = mapa_shared(u_peer, 0);
       int ui = 0;
       bool ok = true;
-      for (int cs = 0; ok && cs < C16; ++cs) {
+      for (int cs = 0; ok && cs < nst; ++cs) {
         const int vs = cs % kNV;
         ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort));
         if (!ok) break;
@@ -989,8 +992,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     }
   } else if (warp == 1) {
     // ---------------- producer: this CTA's weight rows by bulk copy ----------------
-    const int nstages = C16 * kUPerStage;
-    const uint8_t *ublk = U + ((size_t)kblk * 2 + rank) * C16 * NF * P * kCoreBytes;
+    const int nstages = nst * kUPerStage;
+    const uint8_t *ublk = U + ((size_t)kblk * 2 + rank) * C16 * NF * P * kCoreBytes +
+                          (size_t)cs0 * kUPerStage * L::kUStage;
     int issued = 0;
     for (int i = 0; i < nstages; ++i) {
       const int s = i % kNU;
@@ -1045,7 +1049,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     auto load_stage = [&](int cs) {
 #pragma unroll
       for (int q = 0; q < CPT; ++q) {
-        const int c = cs * kCc + cbase + q;
+        const int c = (cs0 + cs) * kCc + cbase + q;
         const bool cok = c < C;
         const Tio *xc = xn + (size_t)c * plane;
 #pragma unroll
@@ -1088,9 +1092,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     // free by then), overlapping the other group's stage and the MMAs.
     bool ok = true;
     if constexpr (M == 2) {
-      if (grp < C16) load_stage(grp);
+      if (grp < nst) load_stage(grp);
     }
-    for (int cs = grp; cs < C16; cs += G::kGroups) {
+    for (int cs = grp; cs < nst; cs += G::kGroups) {
       const int vs = cs % kNV;
       if constexpr (M != 2) load_stage(cs);
       ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
@@ -1150,7 +1154,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       __syncwarp();
       if (lane == 0) mbar_arrive(v_full + 8 * vs);
       if constexpr (M == 2) {
-        if (cs + G::kGroups < C16) load_stage(cs + G::kGroups);
+        if (cs + G::kGroups < nst) load_stage(cs + G::kGroups);
       }
     }
 
@@ -1174,7 +1178,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       const int kq = kblk * G::kCoutCta + (quad * 32) % G::kCoutCta;
       const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
       float *patch = reinterpret_cast<float *>(smem + L::kVOff) + tw * L::kPatchFloats;
-      const float bk = (bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
+      // a split adds its partial sums into y (zeroed by the host; bias and ReLU
+      // follow in a separate pass once every slice has landed)
+      const float bk = (!split && bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
+      const bool do_relu = relu && !split;
       const long long per_img = (long long)tiles_y * tiles_x;
       const int kmax = K - kq < 32 ? K - kq : 32;
 #pragma unroll 1
@@ -1201,7 +1208,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
               if (cf != 0.f) s = fmaf(cf, z[b][e], s);
             }
             s += bk;
-            if (relu) s = s < 0.f ? 0.f : s;
+            if (do_relu) s = s < 0.f ? 0.f : s;
             patch[lane * 33 + e * M + j] = s;
           }
         __syncwarp();
@@ -1213,9 +1220,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
           const int oy = M * yy + irow, ox = M * xx + lane % M;
           if (oy < H && ox < W) {
             Tio *dst = y + ((size_t)nn * K + kq) * plane + (size_t)oy * W + ox;
+            if constexpr (sizeof(Tio) == 4) {
+              if (split) {
 #pragma unroll 4
-            for (int cc = 0; cc < kmax; ++cc)
-              dst[(size_t)cc * plane] = from_f32<Tio>(patch[cc * 33 + lane]);
+                for (int cc = 0; cc < kmax; ++cc)
+                  atomicAdd(reinterpret_cast<float *>(dst + (size_t)cc * plane),
+                            patch[cc * 33 + lane]);
+              } else {
+#pragma unroll 4
+                for (int cc = 0; cc < kmax; ++cc)
+                  dst[(size_t)cc * plane] = from_f32<Tio>(patch[cc * 33 + lane]);
+              }
+            } else {
+#pragma unroll 4
+              for (int cc = 0; cc < kmax; ++cc)
+                dst[(size_t)cc * plane] = from_f32<Tio>(patch[cc * 33 + lane]);
+            }
           }
         }
         __syncwarp();
@@ -1234,23 +1254,70 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
   }
 }
 
+// bias + ReLU over y after a split reduction (fp32, in place)
+__global__ void bias_relu_pass(float *__restrict__ y, const float *__restrict__ bias, int K,
+                               long long plane, long long total, int relu) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    float v = y[i];
+    if (bias) v += bias[(i / plane) % K];
+    if (relu) v = v < 0.f ? 0.f : v;
+    y[i] = v;
+  }
+}
+
+// C_in slices for a layer whose CTA pairs would leave most TPCs idle: each slice
+// keeps at least 2 stages.  1 = no split.
+template <int M>
+static int split_stages(int n, int c, int k, int h, int w, int tpcs, int *per) {
+  using G = PairGeo<M>;
+  const int C16 = (c + kCc - 1) / kCc;
+  const long long tiles = (long long)n * ((h + M - 1) / M) * ((w + M - 1) / M);
+  const long long items = (tiles + G::kN - 1) / G::kN * ((k + G::kCoutCta - 1) / G::kCoutCta);
+  *per = C16;
+  if (2 * items > tpcs || C16 < 4) return 1;
+  long long s = tpcs / items;
+  if (s > C16 / 2) s = C16 / 2;
+  if (s < 2) return 1;
+  *per = (C16 + (int)s - 1) / (int)s;
+  return (C16 + *per - 1) / *per;
+}
+
 template <int M, bool X3, typename Tio>
 static cudaError_t launch_pair(const void *x, const void *U, const float *bias, void *y, int n,
-                               int c, int k, int h, int w, int relu, cudaStream_t s) {
+                               int c, int k, int h, int w, int relu, int allow_split,
+                               cudaStream_t s) {
   using G = PairGeo<M>;
   const int tiles_y = (h + M - 1) / M, tiles_x = (w + M - 1) / M;
   const long long total = (long long)n * tiles_y * tiles_x;
   const long long pairs = (total + G::kN - 1) / G::kN;
   const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
   if (2 * pairs > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidValue;
-  auto fn = wino_fused_tc_pair<M, X3, Tio>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       PairLayout<M, X3>::kSmem);
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  fn<<<dim3((unsigned)(2 * pairs), (unsigned)gy), G::kThreads, PairLayout<M, X3>::kSmem, s>>>(
-      (const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y, tiles_x, total,
-      relu);
-  return cudaGetLastError();
+  int per = (c + kCc - 1) / kCc;
+  const int splits = (allow_split && sizeof(Tio) == 4) ? split_stages<M>(n, c, k, h, w, sms / 2,
+                                                                         &per)
+                                                       : 1;
+  const size_t ybytes = (size_t)n * k * h * w * sizeof(Tio);
+  if (splits > 1 && (e = cudaMemsetAsync(y, 0, ybytes, s)) != cudaSuccess) return e;
+  auto fn = wino_fused_tc_pair<M, X3, Tio>;
+  e = smem_attr_once<wino_fused_tc_pair<M, X3, Tio>>(PairLayout<M, X3>::kSmem);
+  if (e != cudaSuccess) return e;
+  fn<<<dim3((unsigned)(2 * pairs), (unsigned)gy, (unsigned)splits), G::kThreads,
+       PairLayout<M, X3>::kSmem, s>>>((const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k,
+                                       h, w, tiles_y, tiles_x, total, relu, per, splits > 1);
+  if ((e = cudaGetLastError()) != cudaSuccess || splits == 1) return e;
+  if (bias || relu) {
+    cwgk_count_launch();
+    const long long cnt = (long long)n * k * h * w;
+    const unsigned blocks = (unsigned)((cnt + 255) / 256 < 4L * sms ? (cnt + 255) / 256 : 4L * sms);
+    bias_relu_pass<<<blocks, 256, 0, s>>>((float *)y, bias, k, (long long)h * w, cnt, relu);
+    e = cudaGetLastError();
+  }
+  return e;
 }
 
 }  // namespace tc
@@ -1342,9 +1409,17 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
   return 0;
 }
 
+int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant, int bf16,
+                   int allow_split, int sms) {
+  int per = 0;
+  if (variant != CWGK_TC_PAIR || bf16 || !allow_split) return 1;
+  return m == 2 ? tc::split_stages<2>(n, c_in, c_out, h, w, sms / 2, &per)
+                : tc::split_stages<4>(n, c_in, c_out, h, w, sms / 2, &per);
+}
+
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
                  int c_out, int h, int w, int m, int x3, int variant, int bf16, int relu,
-                 void *stream) {
+                 int allow_split, void *stream) {
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
 #define CWG_TC_LAUNCH(X3_, HALF_)                                                              \
@@ -1352,8 +1427,9 @@ int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n
         : tc::launch<X3_, HALF_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
 #define CWG_TC_LAUNCH_PAIR(M_, X3_)                                                             \
   (bf16 ? tc::launch_pair<M_, X3_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu,  \
-                                                   s)                                          \
-        : tc::launch_pair<M_, X3_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
+                                                   allow_split, s)                             \
+        : tc::launch_pair<M_, X3_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu,          \
+                                          allow_split, s))
   if (variant == CWGK_TC_PAIR && m == 2)
     e = x3 ? CWG_TC_LAUNCH_PAIR(2, true) : CWG_TC_LAUNCH_PAIR(2, false);
   else if (variant == CWGK_TC_PAIR && m == 4)

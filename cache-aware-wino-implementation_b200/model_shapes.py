@@ -132,3 +132,44 @@ def run_stack(name: str, n: int, dev, flags: int = 0, keep=None):
     cwg.device_status()
     times = [a.elapsed_time(b) for a, b in ev]
     return times, kept, prepared
+
+
+def capture_stack(name: str, n: int, dev, flags: int = 0):
+    """The same chained stack captured once into a CUDA graph: returns a function that
+    replays every layer's launches (no per-layer host work) and the output buffer of the
+    last layer.  Buffers and transformed weights are allocated up front and stay alive in
+    the closure."""
+    import torch
+
+    import cwg
+
+    bf16 = bool(flags & cwg.BF16)
+    dt = torch.bfloat16 if bf16 else torch.float32
+    flags = flags | cwg.RELU
+    layers = stride1_layers(name)
+    plan, prev, x = [], None, None
+    for i, s in enumerate(layers):
+        g, bias = layer_params(name, i, s, bf16)
+        U = torch.empty(cwg.weight_bytes(s.c_in, s.c_out, 0, flags), dtype=torch.uint8,
+                        device=dev)
+        cwg.weight_transform(torch.from_numpy(g).to(dev), U, s.c_in, s.c_out, 0, flags)
+        if not chains(prev, s):
+            x = torch.from_numpy(stack_input(name, i, n, s, bf16)).to(dev).to(dt)
+        y = torch.empty((n, s.c_out, s.h, s.w), dtype=dt, device=dev)
+        plan.append((s, x, U, torch.from_numpy(bias).to(dev), y))
+        x, prev = y, s
+
+    def launch_all(stream):
+        for s, xi, U, b, yi in plan:
+            cwg.conv3x3_fused(xi, U, b, yi, n, s.c_in, s.c_out, s.h, s.w, 0, flags, stream)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):  # one eager pass sets the kernels' attributes first
+        launch_all(side)
+    torch.cuda.synchronize(dev)
+    cwg.device_status()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        launch_all(torch.cuda.current_stream(dev))
+    return graph.replay, plan[-1][4]

@@ -56,6 +56,9 @@ extern "C" {
                                 accumulators (32-tile blocks) */
 #define CWG_TC_NOPAIR 0x100u /* ablation: single-CTA half-folded tensor-core kernel (64-tile
                                 blocks) instead of the 2-SM pair kernel (128-tile blocks) */
+#define CWG_NO_SPLIT 0x200u  /* bit-reproducible results: never split the C_in reduction of a small
+                                fp32 layer across CTAs (a split adds partial sums atomically, so
+                                the last bits of y vary between runs) */
 
 /* Kernel paths reported by cwg_select. */
 #define CWG_PATH_FFMA 1 /* warp register-blocked FFMA fused kernel */

@@ -100,9 +100,14 @@ def test_selector_f63_runs_on_cuda_cores():
 def test_selector_tensor_core_variants():
     n, c, k, h, w = 4, 128, 256, 30, 30
     tiles = n * 15 * 15
-    pair = cwg.select(n, c, k, h, w)
+    pair = cwg.select(n, c, k, h, w, 2, cwg.NO_SPLIT)
     assert pair.path == cwg.PATH_TC and pair.tiles_per_cta == 128 and pair.tmem_cols == 512
     assert pair.ctas == 2 * (-(-tiles // 128)) * 2  # two CTAs per 128-tile block
+    # 16 (tile block, channel block) items leave most of the 74 TPCs idle: the C_in
+    # reduction (8 stages of 16 channels) splits into 4 slices of 2 stages
+    assert cwg.select(n, c, k, h, w).ctas == pair.ctas * 4
+    assert cwg.select(n, c, k, h, w, 2, cwg.BF16).ctas == pair.ctas  # fp32 layers only
+    assert cwg.select(64, c, k, 56, 56).ctas == cwg.select(64, c, k, 56, 56, 2, cwg.NO_SPLIT).ctas
     single = cwg.select(n, c, k, h, w, 2, cwg.TC_NOPAIR)
     assert single.tiles_per_cta == 64 and single.ctas == (-(-tiles // 64)) * 2
     assert cwg.select(n, c, k, h, w, 2, cwg.TC_FULL16).tiles_per_cta == 32

@@ -21,3 +21,19 @@ def test_model_stack_matches_reference(cuda_dev, name):
         xs = x[:1].float().cpu().numpy()
         ys = y[:1].float().cpu().numpy()
         assert_close(ys, oracle_conv(xs, g, bias, 2, True), "f23", f"{name} layer {i} {s}")
+
+
+def test_model_stack_graph_replay_matches_eager(cuda_dev):
+    """The stack captured into one CUDA graph (launches only, no host work per layer)
+    reproduces the eager stack's final output."""
+    import torch
+
+    import cwg
+
+    name = "resnet18"
+    replay, y_graph = model_shapes.capture_stack(name, 1, cuda_dev, cwg.NO_SPLIT)
+    replay()
+    torch.cuda.synchronize()
+    n_layers = len(model_shapes.stride1_layers(name))
+    _, kept, _ = model_shapes.run_stack(name, 1, cuda_dev, cwg.NO_SPLIT, keep={n_layers - 1})
+    torch.testing.assert_close(y_graph, kept[0][3], rtol=0, atol=0)
