@@ -1178,9 +1178,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       const int kq = kblk * G::kCoutCta + (quad * 32) % G::kCoutCta;
       const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
       float *patch = reinterpret_cast<float *>(smem + L::kVOff) + tw * L::kPatchFloats;
-      // a split adds its partial sums into y (zeroed by the host; bias and ReLU
-      // follow in a separate pass once every slice has landed)
-      const float bk = (!split && bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
+      // a split adds its partial sums into y (zeroed by the host); slice 0 adds
+      // the bias unless a ReLU must follow the full sum, in which case a separate
+      // pass applies both once every slice has landed
+      const bool add_bias = !split || (!relu && blockIdx.z == 0);
+      const float bk = (add_bias && bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
       const bool do_relu = relu && !split;
       const long long per_img = (long long)tiles_y * tiles_x;
       const int kmax = K - kq < 32 ? K - kq : 32;
@@ -1266,8 +1268,10 @@ __global__ void bias_relu_pass(float *__restrict__ y, const float *__restrict__ 
   }
 }
 
-// C_in slices for a layer whose CTA pairs would leave most TPCs idle: each slice
-// keeps at least 2 stages.  1 = no split.
+// C_in slices for a layer whose CTA pairs would leave three quarters of the TPCs
+// idle: each slice keeps at least 2 stages.  1 = no split.  (Above that occupancy
+// the extra zeroing, atomics and bias pass cost more than the shorter C_in loop
+// saves.)
 template <int M>
 static int split_stages(int n, int c, int k, int h, int w, int tpcs, int *per) {
   using G = PairGeo<M>;
@@ -1275,7 +1279,7 @@ static int split_stages(int n, int c, int k, int h, int w, int tpcs, int *per) {
   const long long tiles = (long long)n * ((h + M - 1) / M) * ((w + M - 1) / M);
   const long long items = (tiles + G::kN - 1) / G::kN * ((k + G::kCoutCta - 1) / G::kCoutCta);
   *per = C16;
-  if (2 * items > tpcs || C16 < 4) return 1;
+  if (4 * items > tpcs || C16 < 4) return 1;
   long long s = tpcs / items;
   if (s > C16 / 2) s = C16 / 2;
   if (s < 2) return 1;
@@ -1310,7 +1314,7 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
        PairLayout<M, X3>::kSmem, s>>>((const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k,
                                        h, w, tiles_y, tiles_x, total, relu, per, splits > 1);
   if ((e = cudaGetLastError()) != cudaSuccess || splits == 1) return e;
-  if (bias || relu) {
+  if (relu) {
     cwgk_count_launch();
     const long long cnt = (long long)n * k * h * w;
     const unsigned blocks = (unsigned)((cnt + 255) / 256 < 4L * sms ? (cnt + 255) / 256 : 4L * sms);

@@ -103,9 +103,11 @@ def test_selector_tensor_core_variants():
     pair = cwg.select(n, c, k, h, w, 2, cwg.NO_SPLIT)
     assert pair.path == cwg.PATH_TC and pair.tiles_per_cta == 128 and pair.tmem_cols == 512
     assert pair.ctas == 2 * (-(-tiles // 128)) * 2  # two CTAs per 128-tile block
-    # 16 (tile block, channel block) items leave most of the 74 TPCs idle: the C_in
+    # 16 (tile block, channel block) items leave 3/4 of the 74 TPCs idle: the C_in
     # reduction (8 stages of 16 channels) splits into 4 slices of 2 stages
     assert cwg.select(n, c, k, h, w).ctas == pair.ctas * 4
+    # 25 items (4 images of 56x56) fill a third of the TPCs: no split
+    assert cwg.select(4, c, 128, 56, 56).ctas == cwg.select(4, c, 128, 56, 56, 2, cwg.NO_SPLIT).ctas
     assert cwg.select(n, c, k, h, w, 2, cwg.BF16).ctas == pair.ctas  # fp32 layers only
     assert cwg.select(64, c, k, 56, 56).ctas == cwg.select(64, c, k, 56, 56, 2, cwg.NO_SPLIT).ctas
     single = cwg.select(n, c, k, h, w, 2, cwg.TC_NOPAIR)

@@ -378,24 +378,26 @@ def test_nonfused_ablation_matches_reference(cuda_dev, case):
     assert_close(y.cpu().numpy(), ref, {2: "f23", 4: "f43", 6: "f63"}[m], str(case))
 
 
-@pytest.mark.parametrize("case", [(1, 512, 512, 7, 7, True), (1, 256, 256, 14, 14, False),
-                                  (1, 128, 128, 28, 28, True), (2, 64, 200, 12, 12, True),
-                                  (1, 96, 64, 9, 5, False)],
+@pytest.mark.parametrize("case", [(1, 512, 512, 7, 7, True, True), (1, 256, 256, 14, 14, False, False),
+                                  (1, 128, 128, 28, 28, True, False), (2, 64, 200, 12, 12, True, True),
+                                  (1, 96, 64, 9, 5, True, False), (1, 128, 96, 16, 16, False, True)],
                          ids=lambda c: "x".join(map(str, c)))
 def test_split_reduction_small_layers(cuda_dev, case):
-    """Small fp32 layers split C_in across CTAs (partial sums added into y, then bias and
-    ReLU): same result as the unsplit kernel and the reference."""
-    n, c, k, h, w, use_bias = case
+    """Small fp32 layers split C_in across CTAs (partial sums added into y; bias with
+    slice 0, or bias and ReLU in a second pass): same result as the unsplit kernel and
+    the reference."""
+    n, c, k, h, w, use_bias, relu = case
     rng = np.random.default_rng(sum(case) + 800)
     x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
     g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
     bias = rng.uniform(-0.1, 0.1, k).astype(np.float32) if use_bias else None
     assert cwg.select(n, c, k, h, w).ctas > cwg.select(n, c, k, h, w, 2, cwg.NO_SPLIT).ctas
-    y = gpu_conv(x, g, bias, 2, cwg.RELU, cuda_dev)
-    y1 = gpu_conv(x, g, bias, 2, cwg.RELU | cwg.NO_SPLIT, cuda_dev)
-    y2 = gpu_conv(x, g, bias, 2, cwg.RELU | cwg.NO_SPLIT, cuda_dev)
+    fl = cwg.RELU if relu else 0
+    y = gpu_conv(x, g, bias, 2, fl, cuda_dev)
+    y1 = gpu_conv(x, g, bias, 2, fl | cwg.NO_SPLIT, cuda_dev)
+    y2 = gpu_conv(x, g, bias, 2, fl | cwg.NO_SPLIT, cuda_dev)
     np.testing.assert_array_equal(y1, y2)  # unsplit: bit-reproducible
-    ref = oracle_conv(x, g, bias, 2, True)
+    ref = oracle_conv(x, g, bias, 2, relu)
     assert_close(y, ref, "f23", f"split {case}")
     assert_close(y, y1, "f23", f"split vs unsplit {case}")
 
