@@ -29,6 +29,7 @@
 // returns, and the host reports CWG_ETIMEOUT.
 #include <cstdint>
 
+#include "../../include/cwg.h"
 #include "cwg_common.cuh"
 
 namespace cwg {
@@ -1324,6 +1325,22 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
   return e;
 }
 
+// Diagnostics: one CTA waits, through the kernels' own bounded wait, on an
+// mbarrier that nothing ever arrives on.  After kTimeoutNs the wait gives up,
+// sets g_tc_status and the kernel returns: the host sees CWG_ETIMEOUT and the
+// context stays usable.  No spin is unbounded and nothing faults.
+__global__ void wait_selftest() {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  (void)mbar_wait(smem_u32(&bar), 0, &abort_flag);
+}
+
 }  // namespace tc
 }  // namespace cwg
 
@@ -1452,6 +1469,17 @@ int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n
     return -3;
   }
   return 0;
+}
+
+int cwg_selftest_wait_timeout(void *stream) {
+  tc::wait_selftest<<<1, 32, 0, (cudaStream_t)stream>>>();
+  cwgk_count_launch();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cwgk_set_cuda_error((int)e);
+    return CWG_ECUDA;
+  }
+  return CWG_OK;
 }
 
 int cwgk_read_clear_status(unsigned *status) {

@@ -31,7 +31,7 @@ EXPORTED = (
     "cwg_weight_transform", "cwg_weight_import", "cwg_conv3x3_fused",
     "cwg_host_workspace_bytes", "cwg_conv3x3_fused_host", "cwg_select", "cwg_strerror",
     "cwg_last_cuda_error", "cwg_device_status", "cwg_launch_count", "cwg_version",
-    "cwg_nonfused_workspace_bytes", "cwg_conv3x3_nonfused",
+    "cwg_nonfused_workspace_bytes", "cwg_conv3x3_nonfused", "cwg_selftest_wait_timeout",
 )
 
 
@@ -118,6 +118,8 @@ def lib() -> ctypes.CDLL:
     L.cwg_launch_count.restype = ctypes.c_longlong
     L.cwg_version.argtypes = []
     L.cwg_version.restype = ctypes.c_char_p
+    L.cwg_selftest_wait_timeout.argtypes = [vp]
+    L.cwg_selftest_wait_timeout.restype = i
     L.cwg_nonfused_workspace_bytes.argtypes = [i, i, i, i, i, i]
     L.cwg_nonfused_workspace_bytes.restype = sz
     L.cwg_conv3x3_nonfused.argtypes = [vp, vp, vp, vp, vp, sz, i, i, i, i, i, i, u, vp]
@@ -213,6 +215,12 @@ def conv3x3_fused_host(x_host: int, U, bias, y_host: int, workspace, workspace_b
 def device_status(stream=None) -> None:
     """Raises CwgError(ETIMEOUT) if a bounded device wait gave up since the last check."""
     _check(lib().cwg_device_status(_stream(stream)), "device status")
+
+
+def selftest_wait_timeout(stream=None) -> None:
+    """Launches a kernel whose bounded wait runs out; the next device_status() raises
+    CwgError(ETIMEOUT)."""
+    _check(lib().cwg_selftest_wait_timeout(_stream(stream)), "cwg_selftest_wait_timeout")
 
 
 def launch_count() -> int:

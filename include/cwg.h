@@ -181,6 +181,12 @@ int cwg_last_cuda_error(void);
  * CWG_ECUDA if the synchronisation itself failed). */
 int cwg_device_status(void *stream);
 
+/* Self-test of the failure path: launches one CTA whose bounded device wait can
+ * never complete (an mbarrier nothing arrives on).  After the wait limit (~2 s)
+ * it gives up and sets the status word, so the next cwg_device_status(stream)
+ * returns CWG_ETIMEOUT; the context stays usable.  No reference counterpart. */
+int cwg_selftest_wait_timeout(void *stream);
+
 /* Number of kernel launches this process made through libcwg (all threads). */
 long long cwg_launch_count(void);
 

@@ -402,6 +402,21 @@ def test_split_reduction_small_layers(cuda_dev, case):
     assert_close(y, y1, "f23", f"split vs unsplit {case}")
 
 
+def test_bounded_wait_times_out_and_context_survives(cuda_dev):
+    """A device wait on a barrier nothing arrives on gives up after its limit, the host
+    reads CWG_ETIMEOUT, the status clears, and the next layer runs normally."""
+    cwg.selftest_wait_timeout()
+    with pytest.raises(cwg.CwgError) as e:
+        cwg.device_status()
+    assert e.value.status == cwg.ETIMEOUT
+    cwg.device_status()  # read and cleared
+    rng = np.random.default_rng(15)
+    x = rng.uniform(-1, 1, (1, 64, 12, 12)).astype(np.float32)
+    g = rng.normal(0, 0.05, (64, 64, 3, 3)).astype(np.float32)
+    y = gpu_conv(x, g, None, 2, cwg.RELU, cuda_dev)
+    assert_close(y, oracle_conv(x, g, None, 2, True), "f23", "after a timeout")
+
+
 def test_host_buffer_entry_matches_device_entry(cuda_dev):
     import torch
 
