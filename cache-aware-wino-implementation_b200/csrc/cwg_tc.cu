@@ -124,13 +124,29 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait that may suspend the thread until the phase completes or `hint_ns`
+// elapses: a waiting warp then takes no issue slots or shared-memory
+// bandwidth from the warps that work meanwhile.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kSleepHintNs = 20000;  // longest suspension per try
+
 // Bounded wait: true when the phase completed; false on timeout or when another
 // role already aborted (the abort flag lives in shared memory).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_sleep(bar, parity, kSleepHintNs)) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > kTimeoutNs) {
       *abort = 1;
@@ -726,20 +742,6 @@ __device__ __forceinline__ void mma_pair_bf16(uint32_t d_tmem, uint64_t a_desc, 
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-#pragma unroll
-  for (int e = 0; e < 16; ++e) v[e] = __uint_as_float(r[e]);
-}
-
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   uint32_t r[8];
   asm volatile(
@@ -778,7 +780,7 @@ struct PairGeo {
   static constexpr int kCpt = 2;
   static constexpr int kNU = M == 2 ? 5 : 4;        // weight stages
   static constexpr int kVBytes = kTiles * kCc * 2;  // one frequency of V
-  static constexpr int kEpiTiles = 32 / M;          // tiles per 32-pixel epilogue row
+  static constexpr int kEpiTiles = 32 / M;          // tiles per 32-pixel epilogue patch row
   static_assert(TD * kN <= kTmemCols, "accumulators fit TMEM");
   static_assert(kTiles * kCc == kGroupWarps * 32 * kCpt, "one (tile, channels) per thread");
 };
@@ -837,24 +839,250 @@ struct PairLayout {
   static constexpr int kBarOff = kUOff + kNU * kUStage;
   // v_full[kNV], v_empty[kNV], v_peer[kNV] (rank 0: rank 1's V stage written),
   // u_full[kNU], u_empty[kNU], u_peer[kNU] (rank 0: rank 1's weights landed),
-  // acc_full, drain
-  static constexpr int kNumBars = 3 * kNV + 3 * kNU + 2;
+  // acc_full, drain, tmem_empty (rank 0: both CTAs have read the accumulators)
+  static constexpr int kNumBars = 3 * kNV + 3 * kNU + 3;
   static constexpr int kTmemSlot = kBarOff + 8 * kNumBars;
   static constexpr int kAbortSlot = kTmemSlot + 4;
-  static constexpr int kSmem = kAbortSlot + 4;
-  static constexpr int kPatchFloats = 32 * 33;  // epilogue transpose, per warp
-  // the patches reuse the operand rings once every MMA has completed
-  static_assert(G::kXWarps * kPatchFloats * 4 <= kBarOff, "patches fit the operand rings");
+  // epilogue transpose patch of one warp: 32 output channels x 32 pixels, the
+  // pixel index XOR the channel (conflict-free both ways, no padding)
+  static constexpr int kPx = G::kEpiTiles * M;  // output pixels per patch row
+  static_assert(kPx == 32, "one 32 x 32 patch per warp");
+  static constexpr int kPatchFloats = 32 * 32;
+  static constexpr int kPatchBytes = G::kXWarps * kPatchFloats * 4;
+  // An item's patches live in the V slot that the next item's second stage
+  // takes (free once the item's MMAs have completed); where one V slot is too
+  // small for them (one-product layouts), in a region of their own.
+  static constexpr bool kPatchInV = kPatchBytes <= kVStage;
+  static constexpr int kPatchOff = (kAbortSlot + 4 + 127) / 128 * 128;
+  static constexpr int kSmem = kPatchInV ? kAbortSlot + 4 : kPatchOff + kPatchBytes;
   static_assert(kSmem <= 227 * 1024, "fits the opt-in shared memory of one CTA");
   static_assert(G::NF % kFPerU == 0, "whole frequencies per weight stage");
 };
+
+// Work of one CTA pair p = blockIdx.x / 2, as a sequence of items.
+//   chunk > 0: the tiles [p * chunk, min((p + 1) * chunk, total)), cut into items
+//     of at most kN tiles; each tile block runs for kb_count output-channel
+//     blocks in turn (kb_count == 1: the block blockIdx.y).  A layer of at most
+//     one wave launches chunk = kN, one item per pair; a larger one may launch one
+//     pair per co-resident cluster with equal chunks, so that the last items are
+//     short ones (MMA N rounded up to 16) instead of a last wave that leaves most
+//     TPCs idle.
+//   chunk == 0: round robin over the (kN-tile block, output-channel block) units,
+//     unit u = p + idx * pairs, u = block * kb_count + channel block: the
+//     pairs at work at one time share their input tiles through L2.
+// Either way a pair writes the first stage of its next item ahead of the
+// current item's epilogue.
+struct PairItem {
+  int t0;   // first tile of the item
+  int cnt;       // tiles in the item, 1..kN
+  int kb;        // output-channel block
+};
+template <int KN>
+__device__ __forceinline__ PairItem pair_item(int chunk, int total, int kb_count, int idx) {
+  PairItem it;
+  int hi = total;
+  if (chunk == 0) {
+    const int u = (int)(blockIdx.x >> 1) + idx * (int)(gridDim.x >> 1);
+    const int tb = u / kb_count;
+    it.kb = u - tb * kb_count;
+    it.t0 = tb * KN;
+  } else {
+    const int lo = (int)(blockIdx.x >> 1) * chunk;
+    hi = total - lo > chunk ? lo + chunk : total;
+    const int tbi = idx / kb_count;
+    it.kb = kb_count == 1 ? (int)blockIdx.y : idx - tbi * kb_count;
+    it.t0 = lo + tbi * KN;
+  }
+  const int left = hi - it.t0;
+  it.cnt = left < KN ? left : KN;
+  return it;
+}
+// MMA N of an item (M = 256 takes N in steps of 16); each CTA holds N/2 rows of B
+__device__ __forceinline__ int item_n(int cnt) { return (cnt + 15) & ~15; }
+
+// Named barrier 2: the epilogue warps have finished with their patches.
+constexpr int kBarEpi = 2;
+
+// Epilogue of item e of a pair, run by every transform warp: output rows M ty + i
+// of the item's tiles.  TMEM lane = (il, output channel).  Each group of
+// kEpiTiles tiles (32 output pixels of one row) goes through the warp's patch so
+// that a warp store writes one 128-byte row segment of one channel plane.  Every warp runs every item's epilogue, also after an
+// abort (then only its barrier arrivals), so that the named barriers match.  Not
+// inlined: its registers stay out of the transform loop, which calls it once per
+// item.
+template <int M, bool X3, typename Tio>
+__device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *smem,
+                                           const float *__restrict__ bias, Tio *__restrict__ y,
+                                           int K, int H, int W, int tiles_y, int tiles_x,
+                                           int total_tiles, int chunk, int kb_count,
+                                           int relu, int split) {
+  using L = PairLayout<M, X3>;
+  using G = PairGeo<M>;
+  constexpr int TD = G::TD, kN = G::kN, kNU = L::kNU;
+  constexpr int kEpiThreads = 32 * G::kXWarps;
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t acc_full = sbase + L::kBarOff + 8 * (3 * kNV + 3 * kNU);
+  const uint32_t tmem_empty = acc_full + 16;
+  volatile int *abort = reinterpret_cast<volatile int *>(smem + L::kAbortSlot);
+  const uint32_t *tmem_slot = reinterpret_cast<const uint32_t *>(smem + L::kTmemSlot);
+  const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0);
+  const int lane = threadIdx.x & 31;
+  const int tw = warp - 2;
+  const uint32_t rank = cluster_rank();
+  const size_t plane = (size_t)H * W;
+  const int per_img = tiles_y * tiles_x;
+
+  if (e == 0) named_bar_sync(kBarTmem, 32 + kEpiThreads);  // TMEM address published
+  if (run) run = __all_sync(0xffffffffu, mbar_wait(acc_full, (uint32_t)e & 1u, abort));
+  tc_fence_after();
+  if (run) {
+    constexpr int kE = G::kEpiTiles;
+    const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, e);
+    const uint32_t tmem = *tmem_slot;
+    const int quad = warp & 3;
+    const int il = (quad * 32) / G::kCoutCta;
+    const int irow = (int)rank * G::kRowsI + il;  // output row i of the tile
+    const int col0 = (tw >> 2) * (kN / 4);        // 32 (F2) or 16 (F4) columns per warp
+    const int kq = it.kb * G::kCoutCta + (quad * 32) % G::kCoutCta;
+    const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+    const int pslot = ((e + 1) * nst + 1) % kNV;
+    float *patch =
+        reinterpret_cast<float *>(smem + (L::kPatchInV ? L::kVOff + pslot * L::kVStage
+                                                       : L::kPatchOff)) +
+        tw * L::kPatchFloats;
+    // a split adds its partial sums into y (zeroed by the host); slice 0 adds
+    // the bias unless a ReLU must follow the full sum, in which case a separate
+    // pass applies both once every slice has landed
+    const bool add_bias = !split || (!relu && blockIdx.z == 0);
+    const float bk = (add_bias && bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
+    const bool do_relu = relu && !split;
+    const int kmax = K - kq < 32 ? K - kq : 32;
+#pragma unroll 1
+    for (int gq = 0; gq < (kN / 4) / kE; ++gq) {
+      const int cb = col0 + gq * kE;
+      if (cb >= it.cnt) break;
+      // 8 tiles (columns) at a time from TMEM: TD x 8 registers
+#pragma unroll 1
+      for (int h = 0; h < kE; h += 8) {
+        float z[TD][8];
+#pragma unroll
+        for (int b = 0; b < TD; ++b) tmem_ld8(trow + (uint32_t)(b * kN + cb + h), z[b]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 2 * M; ++q) {  // 4 pixels (px = 4q ..) of this 8-tile half
+          float o[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int e2 = (4 * q + r) / M, j = (4 * q + r) % M;
+            // Y[i][j] = sum_b Z[i][b] At[j][b]
+            float s = 0.f;
+#pragma unroll
+            for (int b = 0; b < TD; ++b) {
+              const float cf = Wino<M>::at(j, b);
+              if (cf != 0.f) s = fmaf(cf, z[b][e2], s);
+            }
+            s += bk;
+            o[r] = do_relu && s < 0.f ? 0.f : s;
+          }
+          const int qg = (h * M) / 4 + q;  // 4-pixel chunk of the 32-pixel row
+          *reinterpret_cast<float4 *>(patch + lane * 32 + ((qg ^ (lane & 7)) << 2)) =
+              make_float4(o[0], o[1], o[2], o[3]);  // lane = channel
+        }
+      }
+      __syncwarp();
+      // lane -> (4-pixel chunk q, channel ch = 4 cc + lane / 8): each lane's
+      // 4 pixels are 4 / M consecutive tiles of the item
+      const int q = lane & 7, chs = lane >> 3;
+      // element offset of the tile's pixel j = 0 in channel kq; -1: no pixel to
+      // store; < -1: -2 - offset of a tile cut by the image's right edge
+      long long off[4 / M];
+      bool all_ok = true;
+#pragma unroll
+      for (int u = 0; u < 4 / M; ++u) {
+        const int tt = cb + (4 * q) / M + u;  // column = tile of the item
+        off[u] = -1;
+        if (tt < it.cnt) {
+          const int TT = it.t0 + tt;
+          const int nn = TT / per_img;
+          const int rem = TT - nn * per_img;
+          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
+          const int oy = M * yy + irow, ox = M * xx;
+          if (oy < H && ox + M <= W)
+            off[u] = ((long long)nn * K + kq) * (long long)plane + (long long)oy * W + ox;
+          else if (oy < H && ox < W)
+            off[u] = -2 - (((long long)nn * K + kq) * (long long)plane + (long long)oy * W + ox);
+        }
+        all_ok = all_ok && off[u] >= 0;
+      }
+      // one vector store when the 4 pixels are contiguous, inside the image and
+      // aligned; else pixel by pixel
+      bool vec = all_ok && ((off[0] & 3) == 0) && ((plane & 3) == 0) &&
+                 ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+#pragma unroll
+      for (int u = 1; u < 4 / M; ++u) vec = vec && off[u] == off[0] + u * M;
+      if (split) vec = false;
+#pragma unroll 2
+      for (int cc = 0; cc < 8; ++cc) {
+        const int ch = 4 * cc + chs;
+        if (ch >= kmax) continue;
+        const float4 v = *reinterpret_cast<const float4 *>(patch + ch * 32 + ((q ^ (ch & 7)) << 2));
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+        if (vec) {
+          Tio *dst = y + off[0] + (long long)ch * plane;
+          if constexpr (sizeof(Tio) == 4) {
+            *reinterpret_cast<float4 *>(dst) = v;
+          } else {
+            uint2 pk;
+            pk.x = pack_bf16(v.x, v.y);
+            pk.y = pack_bf16(v.z, v.w);
+            *reinterpret_cast<uint2 *>(dst) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const long long o0 = off[r / M];
+            if (o0 == -1) continue;
+            const bool part = o0 < -1;  // tile on the image's right edge
+            const long long base = part ? -2 - o0 : o0;
+            const int j = r % M;
+            if (part) {
+              const int ox0 = (int)(base % W);
+              if (ox0 + j >= W) continue;
+            }
+            Tio *dst = y + base + j + (long long)ch * plane;
+            if constexpr (sizeof(Tio) == 4) {
+              if (split)
+                atomicAdd(reinterpret_cast<float *>(dst), vv[r]);
+              else
+                *dst = vv[r];
+            } else {
+              *dst = from_f32<Tio>(vv[r]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+  // this warp's accumulator reads are complete: rank 0 may reuse TMEM
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) {
+    if (rank == 0)
+      mbar_arrive(tmem_empty);
+    else
+      mbar_arrive_cluster(mapa_shared(tmem_empty, 0));
+  }
+  named_bar_sync(kBarEpi, kEpiThreads);  // patches done before the slot takes V
+  return run;
+}
 
 template <int M, bool X3, typename Tio>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads, 1)
     wino_fused_tc_pair(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                        const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
-                       int W, int tiles_y, int tiles_x, long long total_tiles, int relu,
-                       int cs_per_split, int split) {
+                       int W, int tiles_y, int tiles_x, int total_tiles, int relu,
+                       int cs_per_split, int split, int chunk, int kb_count) {
   using L = PairLayout<M, X3>;
   using G = PairGeo<M>;
   constexpr int P = L::kParts, TD = G::TD, NF = G::NF;
@@ -868,7 +1096,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
   const uint32_t v_peer = v_empty + 8 * kNV;
   const uint32_t u_full = v_peer + 8 * kNV, u_empty = u_full + 8 * kNU;
   const uint32_t u_peer = u_empty + 8 * kNU, acc_full = u_peer + 8 * kNU;
-  const uint32_t drain = acc_full + 8;
+  const uint32_t drain = acc_full + 8, tmem_empty = drain + 8;
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::kAbortSlot);
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::kTmemSlot);
 
@@ -879,9 +1107,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
   // this CTA's slice of the C_in reduction (blockIdx.z; one slice unless split)
   const int cs0 = (int)blockIdx.z * cs_per_split;
   const int nst = C16 - cs0 < cs_per_split ? C16 - cs0 : cs_per_split;
-  const int kblk = blockIdx.y;
-  const long long pair0 = (long long)(blockIdx.x >> 1) * kN;  // first tile of the pair
-  const long long tile0 = pair0 + (long long)rank * kTiles;  // this CTA's V columns
+  // this pair's tiles and work items; every role walks the same sequence, and
+  // the pipeline counters run on across items
+  int n_items = 0;
+  if (chunk == 0) {
+    const int units = (total_tiles + kN - 1) / kN * kb_count;
+    const int p = (int)(blockIdx.x >> 1);
+    n_items = p < units ? (units - 1 - p) / (int)(gridDim.x >> 1) + 1 : 0;
+  } else {
+    const int lo = (int)(blockIdx.x >> 1) * chunk;
+    const int hi = total_tiles - lo > chunk ? lo + chunk : total_tiles;
+    n_items = lo < hi ? (hi - lo + kN - 1) / kN * kb_count : 0;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNV; ++i) {
@@ -896,6 +1133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     }
     mbar_init(acc_full, 1);
     mbar_init(drain, 1);
+    mbar_init(tmem_empty, 2 * kXW);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -914,55 +1152,64 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (rank == 0) {
-      constexpr uint32_t idesc = instr_desc(2 * kCout, kN);
       constexpr uint32_t kLo = (uint32_t)(NF * kVBytes) >> 4;  // V hi -> V lo
       const uint64_t a0 = smem_desc(sbase + L::kUOff, 128, 256);
       const uint64_t b0 = smem_desc(sbase + L::kVOff, (uint32_t)(kTiles * 16), 128);
       bool ok = true;
-      int ui = 0;
-      for (int cs = 0; cs < nst; ++cs) {
-        const int vs = cs % kNV;
-        ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort) &&
-                                         mbar_wait(v_peer + 8 * vs, (cs / kNV) & 1, abort));
-        if (!ok) break;
-        tc_fence_after();
-        const uint64_t bst = b0 + (uint64_t)((uint32_t)(vs * L::kVStage) >> 4);
-#pragma unroll 2
-        for (int fp = 0; fp < kUPerStage; ++fp, ++ui) {
-          const int us = ui % kNU;
-          const uint32_t ph = (ui / kNU) & 1;
-          ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, ph, abort) &&
-                                           mbar_wait(u_peer + 8 * us, ph, abort));
+      int ui = 0, g = 0;
+      for (int j = 0; ok && j < n_items; ++j) {
+        const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
+        const uint32_t idesc = instr_desc(2 * kCout, item_n(it.cnt));
+        if (j > 0) {
+          // both CTAs' epilogue warps have read item j-1's accumulators
+          ok = __all_sync(0xffffffffu, mbar_wait(tmem_empty, (j - 1) & 1, abort));
           if (!ok) break;
           tc_fence_after();
-          const uint64_t ast = a0 + (uint64_t)((uint32_t)(us * L::kUStage) >> 4);
+        }
+        for (int cs = 0; cs < nst; ++cs, ++g) {
+          const int vs = g % kNV;
+          ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (g / kNV) & 1, abort) &&
+                                           mbar_wait(v_peer + 8 * vs, (g / kNV) & 1, abort));
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t bst = b0 + (uint64_t)((uint32_t)(vs * L::kVStage) >> 4);
+#pragma unroll 2
+          for (int fp = 0; fp < kUPerStage; ++fp, ++ui) {
+            const int us = ui % kNU;
+            const uint32_t ph = (ui / kNU) & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, ph, abort) &&
+                                             mbar_wait(u_peer + 8 * us, ph, abort));
+            if (!ok) break;
+            tc_fence_after();
+            const uint64_t ast = a0 + (uint64_t)((uint32_t)(us * L::kUStage) >> 4);
 #pragma unroll
-          for (int fi = 0; fi < kFPerU; ++fi) {
-            const int f = fp * kFPerU + fi;
-            const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * kCoreBytes) >> 4);
-            const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
-            // accumulator Z[.][b], b = f % TD; its first term is a = 0 of stage 0
-            const uint32_t d = tmem + (uint32_t)((f % TD) * kN);
-            const uint32_t first = (cs > 0 || f >= TD) ? 1u : 0u;
-            if (elect_one()) mma_pair_bf16(d, ah, bh, idesc, first);
-            if (X3) {
-              if (elect_one()) mma_pair_bf16(d, ah, bh + kLo, idesc, 1u);
-              if (elect_one())
-                mma_pair_bf16(d, ah + (uint64_t)(kCoreBytes >> 4), bh, idesc, 1u);
+            for (int fi = 0; fi < kFPerU; ++fi) {
+              const int f = fp * kFPerU + fi;
+              const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * kCoreBytes) >> 4);
+              const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
+              // accumulator Z[.][b], b = f % TD; its first term is a = 0 of stage 0
+              const uint32_t d = tmem + (uint32_t)((f % TD) * kN);
+              const uint32_t first = (cs > 0 || f >= TD) ? 1u : 0u;
+              if (elect_one()) mma_pair_bf16(d, ah, bh, idesc, first);
+              if (X3) {
+                if (elect_one()) mma_pair_bf16(d, ah, bh + kLo, idesc, 1u);
+                if (elect_one())
+                  mma_pair_bf16(d, ah + (uint64_t)(kCoreBytes >> 4), bh, idesc, 1u);
+              }
             }
+            __syncwarp();
+            if (elect_one()) tc_commit_pair(u_empty + 8 * us, 3);
+            __syncwarp();
           }
-          __syncwarp();
-          if (elect_one()) tc_commit_pair(u_empty + 8 * us, 3);
+          if (!ok) break;
+          if (elect_one()) tc_commit_pair(v_empty + 8 * vs, 3);
           __syncwarp();
         }
         if (!ok) break;
-        if (elect_one()) tc_commit_pair(v_empty + 8 * vs, 3);
-        __syncwarp();
-      }
-      if (ok) {
         if (elect_one()) tc_commit_pair(acc_full, 3);
         __syncwarp();
-      } else {
+      }
+      if (!ok) {
         // drain whatever was issued before giving up (the MMAs read both CTAs)
         if (elect_one()) tc_commit_pair(drain, 1);
         __syncwarp();
@@ -974,40 +1221,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       // relay, in the order rank 0 consumes them: each V stage written and each
       // weight stage landed here -> one arrival on rank 0's barrier.
       const uint32_t v_peer_r0 = mapa_shared(v_peer, 0), u_peer_r0 = mapa_shared(u_peer, 0);
-      int ui = 0;
+      int ui = 0, g = 0;
       bool ok = true;
-      for (int cs = 0; ok && cs < nst; ++cs) {
-        const int vs = cs % kNV;
-        ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (cs / kNV) & 1, abort));
-        if (!ok) break;
-        if (elect_one()) mbar_arrive_cluster(v_peer_r0 + 8 * vs);
-        __syncwarp();
-        for (int fp = 0; fp < kUPerStage; ++fp, ++ui) {
-          const int us = ui % kNU;
-          ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, (ui / kNU) & 1, abort));
+      for (int j = 0; ok && j < n_items; ++j) {
+        for (int cs = 0; ok && cs < nst; ++cs, ++g) {
+          const int vs = g % kNV;
+          ok = __all_sync(0xffffffffu, mbar_wait(v_full + 8 * vs, (g / kNV) & 1, abort));
           if (!ok) break;
-          if (elect_one()) mbar_arrive_cluster(u_peer_r0 + 8 * us);
+          if (elect_one()) mbar_arrive_cluster(v_peer_r0 + 8 * vs);
           __syncwarp();
+          for (int fp = 0; fp < kUPerStage; ++fp, ++ui) {
+            const int us = ui % kNU;
+            ok = __all_sync(0xffffffffu, mbar_wait(u_full + 8 * us, (ui / kNU) & 1, abort));
+            if (!ok) break;
+            if (elect_one()) mbar_arrive_cluster(u_peer_r0 + 8 * us);
+            __syncwarp();
+          }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------- producer: this CTA's weight rows by bulk copy ----------------
-    const int nstages = nst * kUPerStage;
-    const uint8_t *ublk = U + ((size_t)kblk * 2 + rank) * C16 * NF * P * kCoreBytes +
-                          (size_t)cs0 * kUPerStage * L::kUStage;
     int issued = 0;
-    for (int i = 0; i < nstages; ++i) {
-      const int s = i % kNU;
-      if (!__all_sync(0xffffffffu, mbar_wait(u_empty + 8 * s, ((i / kNU) & 1) ^ 1, abort)))
-        break;
-      if (elect_one()) {
-        mbar_expect_tx(u_full + 8 * s, L::kUStage);
-        bulk_g2s(sbase + L::kUOff + s * L::kUStage, ublk + (size_t)i * L::kUStage, L::kUStage,
-                 u_full + 8 * s);
+    bool ok = true;
+    for (int j = 0; ok && j < n_items; ++j) {
+      const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
+      const uint8_t *ublk = U + ((size_t)it.kb * 2 + rank) * C16 * NF * P * kCoreBytes +
+                            (size_t)cs0 * kUPerStage * L::kUStage;
+      for (int q = 0; q < nst * kUPerStage; ++q) {
+        const int s = issued % kNU;
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(u_empty + 8 * s, ((issued / kNU) & 1) ^ 1, abort))) {
+          ok = false;
+          break;
+        }
+        if (elect_one()) {
+          mbar_expect_tx(u_full + 8 * s, L::kUStage);
+          bulk_g2s(sbase + L::kUOff + s * L::kUStage, ublk + (size_t)q * L::kUStage,
+                   L::kUStage, u_full + 8 * s);
+        }
+        __syncwarp();
+        ++issued;
       }
-      __syncwarp();
-      issued = i + 1;
     }
     for (int i = issued - kNU > 0 ? issued - kNU : 0; i < issued; ++i) {
       const int s = i % kNU;
@@ -1016,7 +1271,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       }
     }
   } else {
-    // ---------------- transform warps (this CTA's tiles), then epilogue ----------
+    // ---------------- transform warps (this CTA's tiles) + epilogues ----------------
     const int tw = warp - 2;
     const int grp = tw / G::kGroupWarps, gw = tw % G::kGroupWarps;
     // warp -> (16-tile block, 2*CPT channels); lane -> (tile, CPT channels).  A
@@ -1026,224 +1281,167 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     const int cgrp = gw / kTileBlocks;
     const int cbase = cgrp * (2 * CPT) + (lane & 1) * CPT;
     const int kh = cbase >> 3;
-    const int t = (gw % kTileBlocks) * 16 + (lane >> 1);
-    const long long T = tile0 + t;
-    const bool tile_ok = T < total_tiles;
-    int n = 0, ty = 0, tx = 0;
-    if (tile_ok) {
-      const long long per_img = (long long)tiles_y * tiles_x;
-      n = (int)(T / per_img);
-      const int rem = (int)(T - (long long)n * per_img);
-      ty = rem / tiles_x;
-      tx = rem - ty * tiles_x;
-    }
-    const int y0 = M * ty - 1, x0 = M * tx - 1;
+    const int tb16 = (gw % kTileBlocks) * 16;  // first of the warp's 16 B rows
+    const int t = tb16 + (lane >> 1);          // this lane's B row
     const size_t plane = (size_t)H * W;
-    const Tio *xn = x + (size_t)n * C * plane;
-    bool rv[TD], cv[TD];
+    const int per_img = tiles_y * tiles_x;
+    const int S = n_items * nst;  // every stage of every item, in order
+
+    // The lane's tile in the current item: rank r holds B rows [0, N/2) = the
+    // item's tiles [r N/2, (r + 1) N/2).  A group meets each item first at its
+    // stage 0 or 1.
+    int cnt_cta = 0;
+    unsigned vmask = 0;        // window rows (bits 0..TD-1) / columns (bits 8..) inside the image
+    long long xoff = 0;        // element offset of the window's corner in x, channel 0
+    auto set_item = [&](int j) {
+      const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
+      const int half = item_n(it.cnt) >> 1;
+      const int c = it.cnt - (int)rank * half;
+      cnt_cta = c < 0 ? 0 : (c < half ? c : half);
+      int n = 0, ty = 0, tx = 0;
+      const bool tile_ok = t < cnt_cta;
+      if (tile_ok) {
+        const int T = it.t0 + (int)rank * half + t;
+        n = T / per_img;
+        const int rem = T - n * per_img;
+        ty = rem / tiles_x;
+        tx = rem - ty * tiles_x;
+      }
+      const int y0 = M * ty - 1, x0 = M * tx - 1;
+      xoff = (long long)n * C * (long long)plane + (long long)y0 * W + x0;
+      vmask = 0;
 #pragma unroll
-    for (int i = 0; i < TD; ++i) {
-      rv[i] = tile_ok && (y0 + i) >= 0 && (y0 + i) < H;
-      cv[i] = (x0 + i) >= 0 && (x0 + i) < W;
-    }
+      for (int i = 0; i < TD; ++i) {
+        if (tile_ok && (y0 + i) >= 0 && (y0 + i) < H) vmask |= 1u << i;
+        if ((x0 + i) >= 0 && (x0 + i) < W) vmask |= 256u << i;
+      }
+    };
     float d[CPT][TD][TD];  // [channel][row][col]
-    auto load_stage = [&](int cs) {
+    // input patches of stage s; a lane whose tile is past the item's end loads
+    // nothing (all-zero window mask: every load is predicated off)
+    auto load_stage = [&](int s) {
+      const int j = s / nst, cs = s - j * nst;
+      if (cs < G::kGroups) set_item(j);
 #pragma unroll
       for (int q = 0; q < CPT; ++q) {
         const int c = (cs0 + cs) * kCc + cbase + q;
         const bool cok = c < C;
-        const Tio *xc = xn + (size_t)c * plane;
+        const Tio *xc = x + xoff + (long long)c * (long long)plane;
 #pragma unroll
         for (int i = 0; i < TD; ++i)
 #pragma unroll
-          for (int j = 0; j < TD; ++j)
-            d[q][i][j] = (cok && rv[i] && cv[j])
-                             ? to_f32(xc[(size_t)(y0 + i) * W + (x0 + j)])
-                             : 0.f;
+          for (int j2 = 0; j2 < TD; ++j2)
+            d[q][i][j2] = (cok && ((vmask >> i) & 1u) && ((vmask >> (8 + j2)) & 1u))
+                              ? to_f32(xc[i * W + j2])
+                              : 0.f;
       }
     };
-    // V of frequency f, channels cbase .. cbase+CPT-1 of tile t: 2*CPT bytes per part
+    // V of frequency f, channels cbase .. cbase+CPT-1 of row t: 2*CPT bytes per part
     const uint32_t voff = (uint32_t)(kh * (kTiles * 16) + t * 16 + (cbase & 7) * 2);
     auto put_v = [&](uint8_t *vb, int f, const float (&e)[CPT]) {
-      if constexpr (CPT == 4) {
-        uint2 hi, lo;
-        if (X3) {
-          split_pair(e[0], e[1], hi.x, lo.x);
-          split_pair(e[2], e[3], hi.y, lo.y);
-          *reinterpret_cast<uint2 *>(vb + (NF + f) * kVBytes + voff) = lo;
-        } else {
-          hi.x = pack_bf16(e[0], e[1]);
-          hi.y = pack_bf16(e[2], e[3]);
-        }
-        *reinterpret_cast<uint2 *>(vb + f * kVBytes + voff) = hi;
+      uint32_t hi2, lo2;
+      if (X3) {
+        split_pair(e[0], e[1], hi2, lo2);
+        *reinterpret_cast<uint32_t *>(vb + (NF + f) * kVBytes + voff) = lo2;
       } else {
-        uint32_t hi, lo;
-        if (X3) {
-          split_pair(e[0], e[1], hi, lo);
-          *reinterpret_cast<uint32_t *>(vb + (NF + f) * kVBytes + voff) = lo;
-        } else {
-          hi = pack_bf16(e[0], e[1]);
-        }
-        *reinterpret_cast<uint32_t *>(vb + f * kVBytes + voff) = hi;
+        hi2 = pack_bf16(e[0], e[1]);
       }
+      *reinterpret_cast<uint32_t *>(vb + f * kVBytes + voff) = hi2;
     };
-    // Group g takes the stages cs = g (mod kGroups).  F(2,3): the next stage's
-    // patches load while this one is transformed and stored.  F(4,3): a
-    // stage's patches load before the wait for its V slot (the registers are
-    // free by then), overlapping the other group's stage and the MMAs.
+    static_assert(CPT == 2, "two channels per transform thread");
+
+    // Group g takes the stages s = g (mod kGroups) of the whole sequence.
+    // F(2,3): the next stage's patches load while this one is transformed and
+    // stored.  F(4,3): a stage's patches load before the wait for its V slot
+    // (the registers are free by then), overlapping the other group's stage and
+    // the MMAs.  Item e's epilogue follows the warp's last stage up to item
+    // e+1's first: that stage is written ahead, so the MMAs of item e+1 start as
+    // soon as the accumulators are read.
     bool ok = true;
+    int ep = 0;  // next item whose epilogue this warp owes
     if constexpr (M == 2) {
-      if (grp < nst) load_stage(grp);
+      if (grp < S) load_stage(grp);
     }
-    for (int cs = grp; cs < nst; cs += G::kGroups) {
-      const int vs = cs % kNV;
-      if constexpr (M != 2) load_stage(cs);
-      ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((cs / kNV) & 1) ^ 1, abort));
+    for (int s = grp; s < S; s += G::kGroups) {
+      if (ep < n_items && s > (ep + 1) * nst) {
+        do {
+          ok = pair_epilogue<M, X3, Tio>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
+                                         tiles_x, total_tiles, chunk, kb_count, relu, split) &&
+               ok;
+        } while (ep < n_items && s > (ep + 1) * nst);
+        // F(2,3): this stage's patches were not loaded ahead of the epilogue (their
+        // loads would have queued in front of its stores)
+        if constexpr (M == 2) load_stage(s);
+      }
+      if (!ok) break;
+      const int vs = s % kNV;
+      if constexpr (M != 2) load_stage(s);
+      ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((s / kNV) & 1) ^ 1, abort));
       if (!ok) break;
       uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
-      if constexpr (M == 2) {
-        float v[CPT][TD][TD];
+      if (tb16 < cnt_cta) {
+        if constexpr (M == 2) {
+          float v[CPT][TD][TD];
 #pragma unroll
-        for (int q = 0; q < CPT; ++q) input_transform<M>(d[q], v[q]);
+          for (int q = 0; q < CPT; ++q) input_transform<M>(d[q], v[q]);
 #pragma unroll
-        for (int f = 0; f < NF; ++f) {
-          float e[CPT];
-#pragma unroll
-          for (int q = 0; q < CPT; ++q) e[q] = v[q][f / TD][f % TD];
-          put_v(vb, f, e);
-        }
-      } else {
-        // Bt d Bt^T: the row pass runs in place, then each output row a is
-        // formed, packed and stored, so two 6x6 windows fit the registers.
-#pragma unroll
-        for (int q = 0; q < CPT; ++q)
-#pragma unroll
-          for (int i = 0; i < TD; ++i) {
-            float w[TD];
-#pragma unroll
-            for (int b = 0; b < TD; ++b) {
-              float acc = 0.f;
-#pragma unroll
-              for (int j = 0; j < TD; ++j) {
-                const float cf = Wino<M>::bt(b, j);
-                if (cf != 0.f) acc = fmaf(cf, d[q][i][j], acc);
-              }
-              w[b] = acc;
-            }
-#pragma unroll
-            for (int b = 0; b < TD; ++b) d[q][i][b] = w[b];
-          }
-#pragma unroll
-        for (int a = 0; a < TD; ++a)
-#pragma unroll
-          for (int b = 0; b < TD; ++b) {
+          for (int f = 0; f < NF; ++f) {
             float e[CPT];
 #pragma unroll
-            for (int q = 0; q < CPT; ++q) {
-              float acc = 0.f;
-#pragma unroll
-              for (int i = 0; i < TD; ++i) {
-                const float cf = Wino<M>::bt(a, i);
-                if (cf != 0.f) acc = fmaf(cf, d[q][i][b], acc);
-              }
-              e[q] = acc;
-            }
-            put_v(vb, a * TD + b, e);
+            for (int q = 0; q < CPT; ++q) e[q] = v[q][f / TD][f % TD];
+            put_v(vb, f, e);
           }
+        } else {
+          // Bt d Bt^T: the row pass runs in place, then each output row a is
+          // formed, packed and stored, so two 6x6 windows fit the registers.
+#pragma unroll
+          for (int q = 0; q < CPT; ++q)
+#pragma unroll
+            for (int i = 0; i < TD; ++i) {
+              float w[TD];
+#pragma unroll
+              for (int b = 0; b < TD; ++b) {
+                float acc = 0.f;
+#pragma unroll
+                for (int j = 0; j < TD; ++j) {
+                  const float cf = Wino<M>::bt(b, j);
+                  if (cf != 0.f) acc = fmaf(cf, d[q][i][j], acc);
+                }
+                w[b] = acc;
+              }
+#pragma unroll
+              for (int b = 0; b < TD; ++b) d[q][i][b] = w[b];
+            }
+#pragma unroll
+          for (int a = 0; a < TD; ++a)
+#pragma unroll
+            for (int b = 0; b < TD; ++b) {
+              float e[CPT];
+#pragma unroll
+              for (int q = 0; q < CPT; ++q) {
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < TD; ++i) {
+                  const float cf = Wino<M>::bt(a, i);
+                  if (cf != 0.f) acc = fmaf(cf, d[q][i][b], acc);
+                }
+                e[q] = acc;
+              }
+              put_v(vb, a * TD + b, e);
+            }
+        }
       }
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(v_full + 8 * vs);
       if constexpr (M == 2) {
-        if (cs + G::kGroups < nst) load_stage(cs + G::kGroups);
+        const int sn = s + G::kGroups;
+        if (sn < S && !(ep < n_items && sn > (ep + 1) * nst)) load_stage(sn);
       }
     }
-
-    // ---------------- epilogue: output rows M ty + i of the pair's tiles ----------
-    named_bar_sync(kBarTmem, 32 + kEpiThreads);
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort));
-    tc_fence_after();
-    if (ok) {
-      // TMEM lane = (il, output channel).  Each group of kEpiTiles tiles (32
-      // output pixels of one row) goes through a private patch (row stride 33
-      // floats) so that a warp store writes one contiguous 128-byte row
-      // segment of one channel plane.  Every MMA has completed and every
-      // weight copy landed: the operand rings of this CTA are free.
-      constexpr int kE = G::kEpiTiles;
-      const int quad = warp & 3;
-      const int il = (quad * 32) / G::kCoutCta;
-      const int irow = (int)rank * G::kRowsI + il;  // output row i of the tile
-      const int col0 = (tw >> 2) * (kN / 4);        // 32 (F2) or 16 (F4) tiles per warp
-      const int kq = kblk * G::kCoutCta + (quad * 32) % G::kCoutCta;
-      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
-      float *patch = reinterpret_cast<float *>(smem + L::kVOff) + tw * L::kPatchFloats;
-      // a split adds its partial sums into y (zeroed by the host); slice 0 adds
-      // the bias unless a ReLU must follow the full sum, in which case a separate
-      // pass applies both once every slice has landed
-      const bool add_bias = !split || (!relu && blockIdx.z == 0);
-      const float bk = (add_bias && bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
-      const bool do_relu = relu && !split;
-      const long long per_img = (long long)tiles_y * tiles_x;
-      const int kmax = K - kq < 32 ? K - kq : 32;
-#pragma unroll 1
-      for (int gq = 0; gq < (kN / 4) / kE; ++gq) {
-        const int cb = col0 + gq * kE;
-        float z[TD][kE];
-#pragma unroll
-        for (int b = 0; b < TD; ++b) {
-          if constexpr (kE == 16)
-            tmem_ld16(trow + (uint32_t)(b * kN + cb), z[b]);
-          else
-            tmem_ld8(trow + (uint32_t)(b * kN + cb), z[b]);
-        }
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < kE; ++e)
-#pragma unroll
-          for (int j = 0; j < M; ++j) {
-            // Y[i][j] = sum_b Z[i][b] At[j][b]
-            float s = 0.f;
-#pragma unroll
-            for (int b = 0; b < TD; ++b) {
-              const float cf = Wino<M>::at(j, b);
-              if (cf != 0.f) s = fmaf(cf, z[b][e], s);
-            }
-            s += bk;
-            if (do_relu) s = s < 0.f ? 0.f : s;
-            patch[lane * 33 + e * M + j] = s;
-          }
-        __syncwarp();
-        const long long TT = pair0 + cb + lane / M;
-        if (TT < total_tiles && kmax > 0) {
-          const int nn = (int)(TT / per_img);
-          const int rem = (int)(TT - (long long)nn * per_img);
-          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
-          const int oy = M * yy + irow, ox = M * xx + lane % M;
-          if (oy < H && ox < W) {
-            Tio *dst = y + ((size_t)nn * K + kq) * plane + (size_t)oy * W + ox;
-            if constexpr (sizeof(Tio) == 4) {
-              if (split) {
-#pragma unroll 4
-                for (int cc = 0; cc < kmax; ++cc)
-                  atomicAdd(reinterpret_cast<float *>(dst + (size_t)cc * plane),
-                            patch[cc * 33 + lane]);
-              } else {
-#pragma unroll 4
-                for (int cc = 0; cc < kmax; ++cc)
-                  dst[(size_t)cc * plane] = from_f32<Tio>(patch[cc * 33 + lane]);
-              }
-            } else {
-#pragma unroll 4
-              for (int cc = 0; cc < kmax; ++cc)
-                dst[(size_t)cc * plane] = from_f32<Tio>(patch[cc * 33 + lane]);
-            }
-          }
-        }
-        __syncwarp();
-      }
-    }
+    while (ep < n_items) ok = pair_epilogue<M, X3, Tio>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
+                                           total_tiles, chunk, kb_count, relu, split) && ok;
+    if (n_items == 0) named_bar_sync(kBarTmem, 32 + kEpiThreads);
   }
 
   tc_fence_before();
@@ -1288,16 +1486,79 @@ static int split_stages(int n, int c, int k, int h, int w, int tpcs, int *per) {
   return (C16 + *per - 1) / *per;
 }
 
+// Clusters of a pair kernel that fit on the device at once, cached per device
+// (a TPC whose two SMs are not both free cannot take a pair).
+template <auto Kernel>
+static int resident_pairs(int threads, int smem, int sms) {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return sms / 2;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v > 0) return v;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(sms / 2 * 2), 1, 1);
+  cfg.blockDim = dim3((unsigned)threads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, (const void *)Kernel, &cfg) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    n = sms / 2;
+  }
+  cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+// Work split of a pair launch: pairs, chunk (0: round robin), grid rows,
+// output-channel blocks per pair.  Up to one wave of (tile block, channel block)
+// units, or a split C_in: one unit per pair.  More: one pair per resident
+// cluster, in whichever of the two persistent orders costs less by a simple
+// model of an item's time: a share kFixed (weight stream, A operand reads,
+// epilogue) that does not shrink with the item's tiles, the rest in proportion;
+// plus a prologue (kPrologue of an item) that only the first item pays.
+struct PairPlan {
+  long long pairs, chunk;
+  int gy, kb_count;
+};
+template <int M>
+static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
+  using G = PairGeo<M>;
+  constexpr double kFixed = M == 2 ? 0.5 : 0.75, kPrologue = 0.1;
+  const long long blocks = (total + G::kN - 1) / G::kN, units = blocks * gy;
+  PairPlan p{blocks, G::kN, gy, 1};
+  if (splits > 1 || resident <= 0 || units <= resident) return p;
+  // round robin: every pair takes ceil(units / resident) whole units at most
+  const double rr = (double)((units + resident - 1) / resident) + kPrologue;
+  // equal runs of tiles: whole items plus one short item per channel block
+  double eq = 1e300;
+  // runs start on a multiple of 16 tiles: a lane's pixels then stay in one image
+  // row and aligned for a vector store whenever the row holds an even number of tiles
+  const long long chunk = ((total + resident - 1) / resident + 15) / 16 * 16;
+  if (chunk >= G::kN) {
+    const long long full = chunk / G::kN, rem = chunk % G::kN;
+    eq = (double)gy * ((double)full + (rem ? kFixed + (1 - kFixed) * (double)rem / G::kN : 0.0)) +
+         kPrologue;
+  }
+  if (eq < rr) {
+    p.chunk = chunk;
+    p.pairs = (total + chunk - 1) / chunk;
+  } else {
+    p.chunk = 0;
+    p.pairs = resident;
+  }
+  p.gy = 1;
+  p.kb_count = gy;
+  return p;
+}
+
 template <int M, bool X3, typename Tio>
 static cudaError_t launch_pair(const void *x, const void *U, const float *bias, void *y, int n,
                                int c, int k, int h, int w, int relu, int allow_split,
                                cudaStream_t s) {
   using G = PairGeo<M>;
+  using L = PairLayout<M, X3>;
   const int tiles_y = (h + M - 1) / M, tiles_x = (w + M - 1) / M;
   const long long total = (long long)n * tiles_y * tiles_x;
-  const long long pairs = (total + G::kN - 1) / G::kN;
   const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
-  if (2 * pairs > 0x7fffffffLL || gy > 65535) return cudaErrorInvalidValue;
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1306,14 +1567,20 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
   const int splits = (allow_split && sizeof(Tio) == 4) ? split_stages<M>(n, c, k, h, w, sms / 2,
                                                                          &per)
                                                        : 1;
+  auto fn = wino_fused_tc_pair<M, X3, Tio>;
+  e = smem_attr_once<wino_fused_tc_pair<M, X3, Tio>>(L::kSmem);
+  if (e != cudaSuccess) return e;
+  const int resident = resident_pairs<wino_fused_tc_pair<M, X3, Tio>>(G::kThreads, L::kSmem, sms);
+  const PairPlan plan = plan_pairs<M>(total, gy, splits, resident);
+  // tile indices, item counts and units are 32-bit in the kernel
+  if (total * gy > 0x7fffffffLL || 2 * plan.pairs > 0x7fffffffLL || plan.gy > 65535)
+    return cudaErrorInvalidValue;
   const size_t ybytes = (size_t)n * k * h * w * sizeof(Tio);
   if (splits > 1 && (e = cudaMemsetAsync(y, 0, ybytes, s)) != cudaSuccess) return e;
-  auto fn = wino_fused_tc_pair<M, X3, Tio>;
-  e = smem_attr_once<wino_fused_tc_pair<M, X3, Tio>>(PairLayout<M, X3>::kSmem);
-  if (e != cudaSuccess) return e;
-  fn<<<dim3((unsigned)(2 * pairs), (unsigned)gy, (unsigned)splits), G::kThreads,
-       PairLayout<M, X3>::kSmem, s>>>((const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k,
-                                       h, w, tiles_y, tiles_x, total, relu, per, splits > 1);
+  fn<<<dim3((unsigned)(2 * plan.pairs), (unsigned)plan.gy, (unsigned)splits), G::kThreads,
+       L::kSmem, s>>>((const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y,
+                      tiles_x, (int)total, relu, per, splits > 1, (int)plan.chunk,
+                      plan.kb_count);
   if ((e = cudaGetLastError()) != cudaSuccess || splits == 1) return e;
   if (relu) {
     cwgk_count_launch();

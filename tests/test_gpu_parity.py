@@ -332,6 +332,36 @@ def test_tensor_core_f43_bf16(cuda_dev, case):
     assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", f"bf16 {case}")
 
 
+# Layers above one wave of CTA pairs run persistent pairs: each pair walks an
+# equal run of tiles in items of up to N tiles (the last a short one, MMA N
+# rounded up to 16, possibly empty on the pair's second CTA), every
+# output-channel block per tile block, with the next item's first stage written
+# ahead of the current item's epilogue.
+PERSISTENT = [
+    # n, c, k, h, w, m, flags
+    (13, 64, 136, 56, 56, 2, 0),                    # fp32 F(2,3), 2 ragged channel blocks
+    (13, 64, 64, 56, 56, 2, cwg.BF16),               # bf16 F(2,3): patches outside the V ring
+    (25, 64, 72, 56, 56, 4, cwg.BF16),               # bf16 F(4,3), 2 ragged channel blocks
+]
+
+
+@pytest.mark.parametrize("case", PERSISTENT, ids=lambda c: "x".join(map(str, c[:6])))
+def test_persistent_pairs(cuda_dev, case):
+    n, c, k, h, w, m, extra = case
+    rng = np.random.default_rng(sum(case[:6]) + 900)
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    bf = bool(extra & cwg.BF16)
+    if bf:
+        x, g = workloads.bf16_round(x), workloads.bf16_round(g)
+    ch = cwg.select(n, c, k, h, w, m, cwg.RELU | cwg.FORCE_TC | extra)
+    assert ch.path == cwg.PATH_TC
+    y = gpu_conv(x, g, bias, m, cwg.RELU | cwg.FORCE_TC | extra, cuda_dev)
+    ref = oracle.direct_conv_f64(x, g, bias, True)
+    assert_close(y, ref, "bf16" if bf else "f23", f"persistent {case}")
+
+
 @pytest.mark.parametrize("case", [
     (128, 200, 2, 0), (128, 200, 2, cwg.BF16), (128, 200, 2, cwg.TC_NOPAIR),
     (128, 200, 2, cwg.TC_FULL16), (96, 200, 4, cwg.BF16), (32, 40, 2, 0), (32, 40, 4, cwg.BF16)],
