@@ -124,29 +124,13 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// try_wait that may suspend the thread until the phase completes or `hint_ns`
-// elapses: a waiting warp then takes no issue slots or shared-memory
-// bandwidth from the warps that work meanwhile.
-__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-constexpr uint32_t kSleepHintNs = 20000;  // longest suspension per try
-
 // Bounded wait: true when the phase completed; false on timeout or when another
 // role already aborted (the abort flag lives in shared memory).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
-    if (mbar_try_sleep(bar, parity, kSleepHintNs)) return true;
+    if (mbar_try(bar, parity)) return true;
     if (*abort) return false;
     if (globaltimer() - t0 > kTimeoutNs) {
       *abort = 1;
@@ -754,6 +738,20 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[e]);
 }
 
+// Two consecutive elements (an aligned pair) as fp32; zeros when !ok.
+__device__ __forceinline__ void ld_pair(const float *p, bool ok, float &a, float &b) {
+  float2 v = make_float2(0.f, 0.f);
+  if (ok) v = *reinterpret_cast<const float2 *>(p);
+  a = v.x;
+  b = v.y;
+}
+__device__ __forceinline__ void ld_pair(const __nv_bfloat16 *p, bool ok, float &a, float &b) {
+  uint32_t v = 0;
+  if (ok) v = *reinterpret_cast<const uint32_t *>(p);
+  a = __uint_as_float(v << 16);
+  b = __uint_as_float(v & 0xFFFF0000u);
+}
+
 // Geometry of the pair kernel for F(M x M, 3x3).
 //   F(2,3): rank r holds the 128 rows (i = r, output channel), 64 tiles of V;
 //           N = 128, 4 accumulators Z[r][b] x 128 columns.
@@ -889,8 +887,12 @@ __device__ __forceinline__ PairItem pair_item(int chunk, int total, int kb_count
   } else {
     const int lo = (int)(blockIdx.x >> 1) * chunk;
     hi = total - lo > chunk ? lo + chunk : total;
-    const int tbi = idx / kb_count;
+    int tbi = idx / kb_count;
     it.kb = kb_count == 1 ? (int)blockIdx.y : idx - tbi * kb_count;
+    // odd pairs take their short last block first: the pairs' epilogues (and
+    // their bursts of output stores) then alternate instead of coinciding
+    const int nb = (hi - lo + KN - 1) / KN;
+    if ((blockIdx.x >> 1) & 1) tbi = tbi == 0 ? nb - 1 : tbi - 1;
     it.t0 = lo + tbi * KN;
   }
   const int left = hi - it.t0;
@@ -933,28 +935,29 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
   const int per_img = tiles_y * tiles_x;
 
   if (e == 0) named_bar_sync(kBarTmem, 32 + kEpiThreads);  // TMEM address published
+  // the item and its bias load before the wait for the accumulators
+  const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, e);
+  const int quad = warp & 3;
+  const int kq = it.kb * G::kCoutCta + (quad * 32) % G::kCoutCta;
+  // a split adds its partial sums into y (zeroed by the host); slice 0 adds
+  // the bias unless a ReLU must follow the full sum, in which case a separate
+  // pass applies both once every slice has landed
+  const bool add_bias = !split || (!relu && blockIdx.z == 0);
+  const float bk = (run && add_bias && bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
   if (run) run = __all_sync(0xffffffffu, mbar_wait(acc_full, (uint32_t)e & 1u, abort));
   tc_fence_after();
   if (run) {
     constexpr int kE = G::kEpiTiles;
-    const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, e);
     const uint32_t tmem = *tmem_slot;
-    const int quad = warp & 3;
     const int il = (quad * 32) / G::kCoutCta;
     const int irow = (int)rank * G::kRowsI + il;  // output row i of the tile
     const int col0 = (tw >> 2) * (kN / 4);        // 32 (F2) or 16 (F4) columns per warp
-    const int kq = it.kb * G::kCoutCta + (quad * 32) % G::kCoutCta;
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     const int pslot = ((e + 1) * nst + 1) % kNV;
     float *patch =
         reinterpret_cast<float *>(smem + (L::kPatchInV ? L::kVOff + pslot * L::kVStage
                                                        : L::kPatchOff)) +
         tw * L::kPatchFloats;
-    // a split adds its partial sums into y (zeroed by the host); slice 0 adds
-    // the bias unless a ReLU must follow the full sum, in which case a separate
-    // pass applies both once every slice has landed
-    const bool add_bias = !split || (!relu && blockIdx.z == 0);
-    const float bk = (add_bias && bias != nullptr && kq + lane < K) ? bias[kq + lane] : 0.f;
     const bool do_relu = relu && !split;
     const int kmax = K - kq < 32 ? K - kq : 32;
 #pragma unroll 1
@@ -990,17 +993,17 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
         }
       }
       __syncwarp();
-      // lane -> (4-pixel chunk q, channel ch = 4 cc + lane / 8): each lane's
-      // 4 pixels are 4 / M consecutive tiles of the item
+      // Vector stores: lane -> (4-pixel chunk q, channel 4 cc + lane / 8), each
+      // lane's 4 pixels (4 / M consecutive tiles of the item) contiguous in one
+      // image row and 16-byte aligned.  Otherwise (image edges, odd alignments,
+      // a split's atomics): lane -> pixel, one channel plane per warp store.
       const int q = lane & 7, chs = lane >> 3;
-      // element offset of the tile's pixel j = 0 in channel kq; -1: no pixel to
-      // store; < -1: -2 - offset of a tile cut by the image's right edge
-      long long off[4 / M];
-      bool all_ok = true;
+      long long off0 = -1;  // element offset of the lane's first pixel in channel kq
+      bool vec = !split && ((plane & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
 #pragma unroll
       for (int u = 0; u < 4 / M; ++u) {
         const int tt = cb + (4 * q) / M + u;  // column = tile of the item
-        off[u] = -1;
+        long long o = -1;
         if (tt < it.cnt) {
           const int TT = it.t0 + tt;
           const int nn = TT / per_img;
@@ -1008,27 +1011,20 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
           const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
           const int oy = M * yy + irow, ox = M * xx;
           if (oy < H && ox + M <= W)
-            off[u] = ((long long)nn * K + kq) * (long long)plane + (long long)oy * W + ox;
-          else if (oy < H && ox < W)
-            off[u] = -2 - (((long long)nn * K + kq) * (long long)plane + (long long)oy * W + ox);
+            o = ((long long)nn * K + kq) * (long long)plane + (long long)oy * W + ox;
         }
-        all_ok = all_ok && off[u] >= 0;
+        if (u == 0) off0 = o;
+        vec = vec && o >= 0 && o == off0 + u * M;
       }
-      // one vector store when the 4 pixels are contiguous, inside the image and
-      // aligned; else pixel by pixel
-      bool vec = all_ok && ((off[0] & 3) == 0) && ((plane & 3) == 0) &&
-                 ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
-#pragma unroll
-      for (int u = 1; u < 4 / M; ++u) vec = vec && off[u] == off[0] + u * M;
-      if (split) vec = false;
+      vec = vec && (off0 & 3) == 0;
+      if (__all_sync(0xffffffffu, vec)) {
 #pragma unroll 2
-      for (int cc = 0; cc < 8; ++cc) {
-        const int ch = 4 * cc + chs;
-        if (ch >= kmax) continue;
-        const float4 v = *reinterpret_cast<const float4 *>(patch + ch * 32 + ((q ^ (ch & 7)) << 2));
-        const float vv[4] = {v.x, v.y, v.z, v.w};
-        if (vec) {
-          Tio *dst = y + off[0] + (long long)ch * plane;
+        for (int cc = 0; cc < 8; ++cc) {
+          const int ch = 4 * cc + chs;
+          if (ch >= kmax) continue;
+          const float4 v =
+              *reinterpret_cast<const float4 *>(patch + ch * 32 + ((q ^ (ch & 7)) << 2));
+          Tio *dst = y + off0 + (long long)ch * plane;
           if constexpr (sizeof(Tio) == 4) {
             *reinterpret_cast<float4 *>(dst) = v;
           } else {
@@ -1037,26 +1033,28 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
             pk.y = pack_bf16(v.z, v.w);
             *reinterpret_cast<uint2 *>(dst) = pk;
           }
-        } else {
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            const long long o0 = off[r / M];
-            if (o0 == -1) continue;
-            const bool part = o0 < -1;  // tile on the image's right edge
-            const long long base = part ? -2 - o0 : o0;
-            const int j = r % M;
-            if (part) {
-              const int ox0 = (int)(base % W);
-              if (ox0 + j >= W) continue;
-            }
-            Tio *dst = y + base + j + (long long)ch * plane;
-            if constexpr (sizeof(Tio) == 4) {
-              if (split)
-                atomicAdd(reinterpret_cast<float *>(dst), vv[r]);
-              else
-                *dst = vv[r];
-            } else {
-              *dst = from_f32<Tio>(vv[r]);
+        }
+      } else {
+        const int tt = cb + lane / M, j = lane % M;  // lane = pixel
+        if (tt < it.cnt) {
+          const int TT = it.t0 + tt;
+          const int nn = TT / per_img;
+          const int rem = TT - nn * per_img;
+          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
+          const int oy = M * yy + irow, ox = M * xx + j;
+          if (oy < H && ox < W) {
+            Tio *dst = y + ((size_t)nn * K + kq) * plane + (size_t)oy * W + ox;
+#pragma unroll 4
+            for (int ch = 0; ch < kmax; ++ch) {
+              const float v = patch[ch * 32 + ((((lane >> 2) ^ (ch & 7)) << 2) | (lane & 3))];
+              if constexpr (sizeof(Tio) == 4) {
+                if (split)
+                  atomicAdd(reinterpret_cast<float *>(dst + (size_t)ch * plane), v);
+                else
+                  dst[(size_t)ch * plane] = v;
+              } else {
+                dst[(size_t)ch * plane] = from_f32<Tio>(v);
+              }
             }
           }
         }
@@ -1286,6 +1284,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     const size_t plane = (size_t)H * W;
     const int per_img = tiles_y * tiles_x;
     const int S = n_items * nst;  // every stage of every item, in order
+    // Two-pixel loads need an even row length (every pair then lies inside or
+    // outside the image as a whole) and x aligned to two elements.
+    const bool pairs = ((W & 1) == 0) && ((reinterpret_cast<uintptr_t>(x) & (2 * sizeof(Tio) - 1)) == 0);
 
     // The lane's tile in the current item: rank r holds B rows [0, N/2) = the
     // item's tiles [r N/2, (r + 1) N/2).  A group meets each item first at its
@@ -1315,6 +1316,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
         if (tile_ok && (y0 + i) >= 0 && (y0 + i) < H) vmask |= 1u << i;
         if ((x0 + i) >= 0 && (x0 + i) < W) vmask |= 256u << i;
       }
+      // column pairs (x0 - 1 + 2p, x0 + 2p), p = 0 .. TD/2, for the pair loads
+#pragma unroll
+      for (int p = 0; p <= TD / 2; ++p)
+        if (x0 - 1 + 2 * p >= 0 && x0 + 2 * p < W) vmask |= 65536u << p;
     };
     float d[CPT][TD][TD];  // [channel][row][col]
     // input patches of stage s; a lane whose tile is past the item's end loads
@@ -1327,13 +1332,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
         const int c = (cs0 + cs) * kCc + cbase + q;
         const bool cok = c < C;
         const Tio *xc = x + xoff + (long long)c * (long long)plane;
+        if (pairs) {
+          // TD/2 + 1 aligned two-pixel loads per window row instead of TD
 #pragma unroll
-        for (int i = 0; i < TD; ++i)
+          for (int i = 0; i < TD; ++i) {
+            const Tio *row = xc + i * W - 1;  // column x0 - 1: even
 #pragma unroll
-          for (int j2 = 0; j2 < TD; ++j2)
-            d[q][i][j2] = (cok && ((vmask >> i) & 1u) && ((vmask >> (8 + j2)) & 1u))
-                              ? to_f32(xc[i * W + j2])
-                              : 0.f;
+            for (int p = 0; p <= TD / 2; ++p) {
+              float a0, a1;
+              ld_pair(row + 2 * p, cok && ((vmask >> i) & 1u) && ((vmask >> (16 + p)) & 1u), a0,
+                      a1);
+              if (p > 0) d[q][i][2 * p - 1] = a0;
+              if (p < TD / 2) d[q][i][2 * p] = a1;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < TD; ++i)
+#pragma unroll
+            for (int j2 = 0; j2 < TD; ++j2)
+              d[q][i][j2] = (cok && ((vmask >> i) & 1u) && ((vmask >> (8 + j2)) & 1u))
+                                ? to_f32(xc[i * W + j2])
+                                : 0.f;
+        }
       }
     };
     // V of frequency f, channels cbase .. cbase+CPT-1 of row t: 2*CPT bytes per part
