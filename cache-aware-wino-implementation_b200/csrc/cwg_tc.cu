@@ -738,6 +738,13 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
   for (int e = 0; e < 8; ++e) v[e] = __uint_as_float(r[e]);
 }
 
+// y[0..3] += v, one 16-byte vector reduction in L2 (16-byte aligned address).
+__device__ __forceinline__ void red_add_v4(float *y, float4 v) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(y), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
 // Two consecutive elements (an aligned pair) as fp32; zeros when !ok.
 __device__ __forceinline__ void ld_pair(const float *p, bool ok, float &a, float &b) {
   float2 v = make_float2(0.f, 0.f);
@@ -993,13 +1000,14 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
         }
       }
       __syncwarp();
-      // Vector stores: lane -> (4-pixel chunk q, channel 4 cc + lane / 8), each
-      // lane's 4 pixels (4 / M consecutive tiles of the item) contiguous in one
-      // image row and 16-byte aligned.  Otherwise (image edges, odd alignments,
-      // a split's atomics): lane -> pixel, one channel plane per warp store.
+      // Vector stores (a split: vector reductions): lane -> (4-pixel chunk q,
+      // channel 4 cc + lane / 8), each lane's 4 pixels (4 / M consecutive tiles
+      // of the item) contiguous in one image row and 16-byte aligned.
+      // Otherwise (image edges, odd alignments): lane -> pixel, one channel
+      // plane per warp store.
       const int q = lane & 7, chs = lane >> 3;
       long long off0 = -1;  // element offset of the lane's first pixel in channel kq
-      bool vec = !split && ((plane & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
+      bool vec = ((plane & 3) == 0) && ((reinterpret_cast<uintptr_t>(y) & 15) == 0);
 #pragma unroll
       for (int u = 0; u < 4 / M; ++u) {
         const int tt = cb + (4 * q) / M + u;  // column = tile of the item
@@ -1026,7 +1034,10 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
               *reinterpret_cast<const float4 *>(patch + ch * 32 + ((q ^ (ch & 7)) << 2));
           Tio *dst = y + off0 + (long long)ch * plane;
           if constexpr (sizeof(Tio) == 4) {
-            *reinterpret_cast<float4 *>(dst) = v;
+            if (split)
+              red_add_v4(reinterpret_cast<float *>(dst), v);
+            else
+              *reinterpret_cast<float4 *>(dst) = v;
           } else {
             uint2 pk;
             pk.x = pack_bf16(v.x, v.y);
@@ -1044,8 +1055,13 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
           const int oy = M * yy + irow, ox = M * xx + j;
           if (oy < H && ox < W) {
             Tio *dst = y + ((size_t)nn * K + kq) * plane + (size_t)oy * W + ox;
+            // the slices of a split start on different channels, so that their
+            // atomic adds do not meet on the same lines at the same time
+            const int rot = split ? (int)(blockIdx.z * 8) & 31 : 0;
 #pragma unroll 4
-            for (int ch = 0; ch < kmax; ++ch) {
+            for (int c2 = 0; c2 < 32; ++c2) {
+              const int ch = (c2 + rot) & 31;
+              if (ch >= kmax) continue;
               const float v = patch[ch * 32 + ((((lane >> 2) ^ (ch & 7)) << 2) | (lane & 3))];
               if constexpr (sizeof(Tio) == 4) {
                 if (split)
