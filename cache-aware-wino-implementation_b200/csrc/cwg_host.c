@@ -419,9 +419,37 @@ static int pipe_ready(tile_ctx *c) {
 /* Large layers: the batch is cut into image chunks; chunk i's copy-in (copy
  * stream), convolution (caller's stream) and copy-out (second copy stream)
  * overlap with the neighbouring chunks, so the call costs about one
- * direction of host<->device traffic instead of both plus the kernel. */
+ * direction of host<->device traffic instead of both plus the kernel.  Chunk
+ * sizes ramp up (1, 2, 4, ... images) to the steady size and back down at the
+ * end: the first copy-in and the last copy-out, which nothing overlaps, stay
+ * short. */
 #define HOST_PIPE_MIN_BYTES (8u << 20)
-#define HOST_PIPE_CHUNKS 16
+#define HOST_PIPE_STEADY 12 /* steady chunks: about n / 12 images each */
+#define HOST_PIPE_MAX_CHUNKS 64
+
+/* Chunk sizes for n images; returns the number of chunks (<= HOST_PIPE_MAX_CHUNKS). */
+static int pipe_chunks(int n, int *sizes) {
+  int steady = n / HOST_PIPE_STEADY;
+  if (steady < 1) steady = 1;
+  int head[8], nh = 0;
+  for (int r = 1; r < steady && nh < 8; r *= 2) head[nh++] = r;
+  int ramp = 0;
+  for (int i = 0; i < nh; ++i) ramp += 2 * head[i];
+  while (nh > 0 && ramp > n) {  /* batch too small for the full ramp */
+    --nh;
+    ramp -= 2 * head[nh];
+  }
+  int k = 0;
+  for (int i = 0; i < nh; ++i) sizes[k++] = head[i];
+  int mid = n - ramp;
+  const int nmid = mid > 0 ? (mid + steady - 1) / steady : 0;
+  for (int i = 0; i < nmid && k < HOST_PIPE_MAX_CHUNKS - nh; ++i) {
+    const int cnt = (mid - (mid / nmid) * nmid > i) ? mid / nmid + 1 : mid / nmid;
+    sizes[k++] = cnt;
+  }
+  for (int i = nh - 1; i >= 0; --i) sizes[k++] = head[i];
+  return k;
+}
 
 int cwg_conv3x3_fused_host(const void *x_host, const void *U, const float *bias, void *y_host,
                            void *workspace, size_t workspace_bytes, int n, int c_in, int c_out,
@@ -445,7 +473,8 @@ int cwg_conv3x3_fused_host(const void *x_host, const void *U, const float *bias,
   rc = pipe_ready(c);
   if (rc) return rc;
   const size_t xi = xbytes / (size_t)n, yi = ybytes / (size_t)n;  /* bytes per image */
-  const int chunks = n < HOST_PIPE_CHUNKS ? n : HOST_PIPE_CHUNKS;
+  int sizes[HOST_PIPE_MAX_CHUNKS];
+  const int chunks = pipe_chunks(n, sizes);
   /* everything already queued on the caller's stream comes first */
   cudaError_t e = cudaEventRecord(c->ev_start, s);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_in, c->ev_start, 0);
@@ -453,7 +482,7 @@ int cwg_conv3x3_fused_host(const void *x_host, const void *U, const float *bias,
   if (e != cudaSuccess) return cuda_fail(e);
   int done = 0;
   for (int i = 0; i < chunks; ++i) {
-    const int cnt = (n - done) / (chunks - i);
+    const int cnt = sizes[i];
     const size_t xo = (size_t)done * xi, yo = (size_t)done * yi;
     e = cudaMemcpyAsync(xd + xo, (const char *)x_host + xo, (size_t)cnt * xi,
                         cudaMemcpyHostToDevice, c->s_in);
