@@ -783,7 +783,7 @@ struct PairGeo {
   static constexpr int kGroups = M == 2 ? 1 : 2;
   static constexpr int kGroupWarps = kXWarps / kGroups;
   static constexpr int kCpt = 2;
-  static constexpr int kNU = M == 2 ? 5 : 4;        // weight stages
+  static constexpr int kNU = 5;                     // weight stages
   static constexpr int kVBytes = kTiles * kCc * 2;  // one frequency of V
   static constexpr int kEpiTiles = 32 / M;          // tiles per 32-pixel epilogue patch row
   static_assert(TD * kN <= kTmemCols, "accumulators fit TMEM");
