@@ -422,7 +422,8 @@ def main() -> None:
                           choice.path == cwg.PATH_TC else "fp32 FFMA")),
                 "l2": f"{nsets} rotating x/y buffer sets ({nsets * (xbytes + ybytes) / 2**20:.0f}"
                       " MiB) > 126 MiB L2",
-                "ctas": choice.ctas, "tiles_per_cta": choice.tiles_per_cta,
+                "ctas": choice.ctas, "ctas_launched": choice.ctas_launched,
+                "order": choice.order_name, "tiles_per_cta": choice.tiles_per_cta,
                 "cout_per_cta": choice.cout_per_cta}),
             "roofline": roof,
             "e2e": None if te_ms is None else {

@@ -234,6 +234,14 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
                 t.ctas_per_tile_block *
                 cwgk_tc_splits(n, c_in, c_out, h, w, mm, tc_variant(flags),
                                (flags & CWG_BF16) != 0, !(flags & CWG_NO_SPLIT), num_sms());
+    out->ctas_launched = out->ctas;
+    out->order = CWG_ORDER_GRID;
+    if (n > 0 && cwgk_tc_plan(n, c_in, c_out, h, w, mm, tc_x3(mm, flags), tc_variant(flags),
+                              (flags & CWG_BF16) != 0, !(flags & CWG_NO_SPLIT), num_sms(),
+                              &out->ctas_launched, &out->order) != 0) {
+      out->ctas_launched = out->ctas;
+      out->order = CWG_ORDER_GRID;
+    }
   } else {
     cwgk_ffma_cfg c;
     if (pick_ffma(n, c_out, h, w, mm, &c) < 0) return CWG_EUNSUPPORTED;
@@ -245,6 +253,8 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
     out->tmem_cols = 0;
     out->ctas = (long long)n * ((th + c.ty - 1) / c.ty) * ((tw + c.tx - 1) / c.tx) *
                 ((c_out + c.kb - 1) / c.kb);
+    out->ctas_launched = out->ctas;
+    out->order = CWG_ORDER_GRID;
   }
   if (out->smem_bytes > SMEM_LIMIT || out->tmem_cols > 512) return CWG_EUNSUPPORTED;
   return CWG_OK;

@@ -78,6 +78,10 @@ int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n
 /* C_in slices the tensor-core path uses for this layer (1 = no split). */
 int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant, int bf16,
                    int allow_split, int sms);
+/* The pair kernel's launch plan for a layer on the current device (or, without
+ * one, `sms` SMs): CTAs launched and CWG_ORDER_*. */
+int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int x3, int variant, int bf16,
+                 int allow_split, int sms, long long *ctas, int *order);
 
 /* Per-tile kernel on device buffers (reference layouts). */
 int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,

@@ -1555,13 +1555,14 @@ static int resident_pairs(int threads, int smem, int sms) {
 struct PairPlan {
   long long pairs, chunk;
   int gy, kb_count;
+  int order;  // CWG_ORDER_*
 };
 template <int M>
 static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
   using G = PairGeo<M>;
   constexpr double kFixed = M == 2 ? 0.5 : 0.75, kPrologue = 0.1;
   const long long blocks = (total + G::kN - 1) / G::kN, units = blocks * gy;
-  PairPlan p{blocks, G::kN, gy, 1};
+  PairPlan p{blocks, G::kN, gy, 1, CWG_ORDER_GRID};
   if (splits > 1 || resident <= 0 || units <= resident) return p;
   // round robin: every pair takes ceil(units / resident) whole units at most
   const double rr = (double)((units + resident - 1) / resident) + kPrologue;
@@ -1578,9 +1579,11 @@ static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
   if (eq < rr) {
     p.chunk = chunk;
     p.pairs = (total + chunk - 1) / chunk;
+    p.order = CWG_ORDER_RUNS;
   } else {
     p.chunk = 0;
     p.pairs = resident;
+    p.order = CWG_ORDER_ROUND;
   }
   p.gy = 1;
   p.kb_count = gy;
@@ -1627,6 +1630,29 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
     e = cudaGetLastError();
   }
   return e;
+}
+
+// The launch plan of a layer as launch_pair would make it on the current device
+// (without one: `sms` SMs and one cluster per TPC).
+template <int M, bool X3, typename Tio>
+static void plan_layer(int n, int c, int k, int h, int w, int allow_split, int sms,
+                       long long *ctas, int *order) {
+  using G = PairGeo<M>;
+  using L = PairLayout<M, X3>;
+  const long long total = (long long)n * ((h + M - 1) / M) * ((w + M - 1) / M);
+  const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
+  int per = 0;
+  const int splits =
+      (allow_split && sizeof(Tio) == 4) ? split_stages<M>(n, c, k, h, w, sms / 2, &per) : 1;
+  int resident = sms / 2, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess &&
+      smem_attr_once<wino_fused_tc_pair<M, X3, Tio>>(L::kSmem) == cudaSuccess)
+    resident = resident_pairs<wino_fused_tc_pair<M, X3, Tio>>(G::kThreads, L::kSmem, sms);
+  else
+    (void)cudaGetLastError();
+  const PairPlan p = plan_pairs<M>(total, gy, splits, resident);
+  *ctas = 2 * p.pairs * p.gy * splits;
+  *order = p.order;
 }
 
 // Diagnostics: one CTA waits, through the kernels' own bounded wait, on an
@@ -1740,6 +1766,26 @@ int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant,
   if (variant != CWGK_TC_PAIR || bf16 || !allow_split) return 1;
   return m == 2 ? tc::split_stages<2>(n, c_in, c_out, h, w, sms / 2, &per)
                 : tc::split_stages<4>(n, c_in, c_out, h, w, sms / 2, &per);
+}
+
+int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int x3, int variant, int bf16,
+                 int allow_split, int sms, long long *ctas, int *order) {
+  if (variant != CWGK_TC_PAIR || !(m == 2 || m == 4)) return -1;
+#define CWG_PLAN(M_, X3_, T_) \
+  tc::plan_layer<M_, X3_, T_>(n, c_in, c_out, h, w, allow_split, sms, ctas, order)
+  if (m == 2) {
+    if (bf16)
+      x3 ? CWG_PLAN(2, true, __nv_bfloat16) : CWG_PLAN(2, false, __nv_bfloat16);
+    else
+      x3 ? CWG_PLAN(2, true, float) : CWG_PLAN(2, false, float);
+  } else {
+    if (bf16)
+      x3 ? CWG_PLAN(4, true, __nv_bfloat16) : CWG_PLAN(4, false, __nv_bfloat16);
+    else
+      x3 ? CWG_PLAN(4, true, float) : CWG_PLAN(4, false, float);
+  }
+#undef CWG_PLAN
+  return 0;
 }
 
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,

@@ -25,6 +25,7 @@ OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, ENOMEM, ENODEV = 0, -1, -2, -3, -4, -
 RELU, BF16, FORCE_FFMA, FORCE_TC, TC_SINGLE, TC_FULL16 = 0x1, 0x2, 0x10, 0x20, 0x40, 0x80
 TC_NOPAIR, NO_SPLIT = 0x100, 0x200
 PATH_FFMA, PATH_TC = 1, 2
+ORDER_GRID, ORDER_RUNS, ORDER_ROUND = 0, 1, 2  # cwg_choice.order
 
 EXPORTED = (
     "fused_winograd_f23", "cwg_tiles_fused", "cwg_last_status", "cwg_weight_bytes",
@@ -49,7 +50,8 @@ class cwg_choice(ctypes.Structure):
         ("cout_per_cta", ctypes.c_int), ("cin_chunk", ctypes.c_int), ("threads", ctypes.c_int),
         ("smem_bytes", ctypes.c_int), ("tmem_cols", ctypes.c_int), ("ctas", ctypes.c_longlong),
         ("gemm_flops", ctypes.c_double), ("alg_bytes", ctypes.c_double),
-        ("mma_products", ctypes.c_int),
+        ("mma_products", ctypes.c_int), ("ctas_launched", ctypes.c_longlong),
+        ("order", ctypes.c_int),
     ]
 
 
@@ -67,10 +69,17 @@ class Choice:
     gemm_flops: float
     alg_bytes: float
     mma_products: int
+    ctas_launched: int
+    order: int
 
     @property
     def path_name(self) -> str:
         return {PATH_FFMA: "ffma", PATH_TC: "tcgen05"}.get(self.path, "?")
+
+    @property
+    def order_name(self) -> str:
+        return {ORDER_GRID: "one unit per CTA pair", ORDER_RUNS: "persistent pairs, equal tile runs",
+                ORDER_ROUND: "persistent pairs, round robin"}.get(self.order, "?")
 
 
 _lib = None

@@ -80,7 +80,17 @@ typedef struct cwg_choice {
   double alg_bytes;  /* x + y + U + bias, each touched once */
   int mma_products;  /* bf16 tensor-core products per multiply-accumulate: 3 (hi/lo split,
                         fp32-accurate) or 1; 0 on the FFMA path */
+  long long ctas_launched; /* CTAs the launch really uses: `ctas`, or for a layer larger than
+                              one wave of CTA pairs, two per co-resident cluster of the current
+                              device (B200's 74 TPCs when no device is present) */
+  int order;         /* CWG_ORDER_*: how the tensor-core kernel walks its work */
 } cwg_choice;
+
+/* cwg_choice.order */
+#define CWG_ORDER_GRID 0  /* one work unit (tile block x channel block x C_in slice) per CTA
+                             or CTA pair */
+#define CWG_ORDER_RUNS 1  /* persistent pairs, each an equal run of tiles */
+#define CWG_ORDER_ROUND 2 /* persistent pairs, round robin over the work units */
 
 /* ---- reference-compatible per-tile entry points (HOST pointers) ----------- */
 

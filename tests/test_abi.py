@@ -14,6 +14,12 @@ HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
                       "cwg.h")
 
 
+
+def cuda_present() -> bool:
+    import torch
+
+    return torch.cuda.is_available()
+
 def declared_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
@@ -121,6 +127,29 @@ def test_selector_tensor_core_variants():
     with pytest.raises(cwg.CwgError) as e:
         cwg.select(n, c, k, h, w, 2, cwg.TC_NOPAIR | cwg.TC_FULL16)
     assert e.value.status == cwg.EINVAL
+
+
+def test_selector_launch_plan():
+    """Which grid the pair kernel launches (without a device: 74 TPCs, one cluster each)."""
+    small = cwg.select(4, 128, 128, 56, 56)  # 25 tile blocks: one per CTA pair
+    assert small.order == cwg.ORDER_GRID and small.ctas_launched == small.ctas == 50
+    # config 3: 392 blocks = 5.3 waves -> 73 persistent pairs, each 688 tiles (5 x 128 + 48)
+    c3 = cwg.select(64, 128, 128, 56, 56)
+    assert c3.ctas == 784
+    if not cuda_present():
+        assert c3.order == cwg.ORDER_RUNS and c3.ctas_launched == 146
+    assert c3.order in (cwg.ORDER_RUNS, cwg.ORDER_ROUND) and c3.ctas_launched < c3.ctas
+    # config 5 (F(4,3), 4 channel blocks): round robin over (tile block, channel block) units
+    c5 = cwg.select(128, 256, 256, 112, 112, 4, cwg.BF16)
+    assert c5.ctas == 2 * 1568 * 4
+    if not cuda_present():
+        assert c5.order == cwg.ORDER_ROUND and c5.ctas_launched == 148
+    # a split C_in keeps one unit per pair; so does the CUDA-core path
+    split = cwg.select(1, 512, 512, 7, 7)
+    assert split.order == cwg.ORDER_GRID and split.ctas_launched == split.ctas
+    ffma = cwg.select(1, 16, 32, 56, 56)
+    assert ffma.path == cwg.PATH_FFMA and ffma.order == cwg.ORDER_GRID
+    assert ffma.ctas_launched == ffma.ctas
 
 
 def test_selector_f43_tensor_core():
