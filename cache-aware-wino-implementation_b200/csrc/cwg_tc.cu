@@ -1,8 +1,10 @@
 // cwg_tc.cu -- the tcgen05/TMEM fused Winograd F(2x2,3x3) kernels (sm_100a).
 //
 // wino_fused_tc_pair (default; defined after the single-CTA kernel): a 2-SM CTA
-// pair computes 128 output channels x 128 output tiles with
-// tcgen05.mma.cta_group::2; see the comment above it.
+// pair computes items of up to 128 output tiles x 128 output channels (F(2,3)) with
+// tcgen05.mma.cta_group::2; a layer larger than one wave runs one persistent pair
+// per co-resident cluster, which writes its next item's first stage while the
+// current item's epilogue drains TMEM; see the comments above it.
 //
 // wino_fused_tc (ablations CWG_TC_NOPAIR / CWG_TC_FULL16): one CTA computes 128
 // output channels x 64 (half-folded) or 32 (16 accumulators) output tiles:
