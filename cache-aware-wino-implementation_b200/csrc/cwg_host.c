@@ -434,7 +434,7 @@ static int pipe_ready(tile_ctx *c) {
  * end: the first copy-in and the last copy-out, which nothing overlaps, stay
  * short. */
 #define HOST_PIPE_MIN_BYTES (8u << 20)
-#define HOST_PIPE_STEADY 12 /* steady chunks: about n / 12 images each */
+#define HOST_PIPE_STEADY 5 /* steady chunks: about n / 5 images each */
 #define HOST_PIPE_MAX_CHUNKS 64
 
 /* Chunk sizes for n images; returns the number of chunks (<= HOST_PIPE_MAX_CHUNKS). */
