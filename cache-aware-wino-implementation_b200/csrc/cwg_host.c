@@ -79,11 +79,13 @@ static int num_sms(void) {
 /* ---- path decision (depends only on c_in, c_out, m, flags, so that the
  * weight layout chosen at transform time matches the conv call) ----------- */
 /* Tensor-core kernel variant: the 2-SM pair kernel unless a flag asks for one
- * of the single-CTA kernels. */
-static int tc_variant(unsigned flags) {
+ * of the single-CTA kernels; F(2,3) layers of at most 64 output channels run
+ * the pair kernel with M = 128 (64 channels per CTA), which reads and streams
+ * half the weight rows of the M = 256 kernel, whose other half would be zero. */
+static int tc_variant(unsigned flags, int m, int c_out) {
   if (flags & CWG_TC_FULL16) return CWGK_TC_FULL16;
   if (flags & CWG_TC_NOPAIR) return CWGK_TC_HALF;
-  return CWGK_TC_PAIR;
+  return (m == 2 && c_out <= 64) ? CWGK_TC_PAIR64 : CWGK_TC_PAIR;
 }
 
 /* Products per multiply-accumulate on the tensor cores: 3 (bf16 hi/lo split,
@@ -99,10 +101,10 @@ static int tc_x3(int m, unsigned flags) {
 /* F(4,3) runs on the tensor cores for bf16 layers only: with fp32 data the
  * hi/lo split's dropped lo*lo terms, amplified by the output transform, leave
  * ~4e-4 absolute error against fp32 F(4,3) -- outside the fp32 parity bar. */
-static int tc_available(int m, unsigned flags) {
+static int tc_available(int m, unsigned flags, int c_out) {
   cwgk_tc_cfg cfg;
   if (m == 4 && !(flags & CWG_BF16)) return 0;
-  return cwgk_tc_get_cfg(tc_x3(m, flags), tc_variant(flags), m, &cfg) == 0;
+  return cwgk_tc_get_cfg(tc_x3(m, flags), tc_variant(flags, m, c_out), m, &cfg) == 0;
 }
 
 /* Tensor cores only where the per-frequency GEMM is a real contraction: both
@@ -118,7 +120,7 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
   if ((flags & CWG_TC_FULL16) && (flags & CWG_TC_NOPAIR)) return CWG_EINVAL;
   /* the tensor-core path runs F(2,3) unless F(4,3) is asked for */
   const int m_tc = m ? m : 2;
-  const int tc_ok = tc_shape_ok(c_in, c_out) && tc_available(m_tc, flags);
+  const int tc_ok = tc_shape_ok(c_in, c_out) && tc_available(m_tc, flags, c_out);
   if (flags & CWG_FORCE_TC) {
     if (!tc_ok) return CWG_EUNSUPPORTED;
     *m_out = m_tc;
@@ -139,10 +141,12 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
   return CWG_OK;
 }
 
-static int layout_of(int path, int m, unsigned flags) {
+static int layout_of(int path, int m, unsigned flags, int c_out) {
   if (path == CWG_PATH_TC) {
     const int x3 = tc_x3(m, flags);
-    if (tc_variant(flags) == CWGK_TC_PAIR) return x3 ? CWGK_LAYOUT_TC2_X3 : CWGK_LAYOUT_TC2_X1;
+    const int v = tc_variant(flags, m, c_out);
+    if (v == CWGK_TC_PAIR) return x3 ? CWGK_LAYOUT_TC2_X3 : CWGK_LAYOUT_TC2_X1;
+    if (v == CWGK_TC_PAIR64) return x3 ? CWGK_LAYOUT_TC2H_X3 : CWGK_LAYOUT_TC2H_X1;
     return x3 ? CWGK_LAYOUT_TC_X3 : CWGK_LAYOUT_TC_X1;
   }
   /* The CUDA-core kernel keeps U in fp32 for bf16 layers too: rounding U to
@@ -157,17 +161,25 @@ static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
     case CWGK_LAYOUT_TC_X3:
     case CWGK_LAYOUT_TC_X1:
     case CWGK_LAYOUT_TC2_X3:
-    case CWGK_LAYOUT_TC2_X1: {
-      /* [ceil(C_out / kb)][sets][C_pad / 16][nf][parts] blocks of 128 rows x 16
-       * channels (4096 bytes).  Pair layout: one set per rank, and a block's 128
-       * rows are m/2 output rows x kb = 128 / (m/2) channels. */
-      const int pair = layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
-      const size_t kb = pair ? (size_t)(128 / (m / 2)) : 128;
+    case CWGK_LAYOUT_TC2_X1:
+    case CWGK_LAYOUT_TC2H_X3:
+    case CWGK_LAYOUT_TC2H_X1: {
+      /* [ceil(C_out / kb)][sets][C_pad / 16][nf][parts] blocks of `rows` rows x
+       * 16 channels (rows x 32 bytes).  Pair layouts: one set per rank, and a
+       * block's rows are m/2 output rows x kb = rows / (m/2) channels; 128 rows,
+       * or 64 for the 64-channel pair kernel. */
+      const int half = layout == CWGK_LAYOUT_TC2H_X3 || layout == CWGK_LAYOUT_TC2H_X1;
+      const int pair = half || layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
+      const size_t rows = half ? 64 : 128;
+      const size_t kb = pair ? rows / (size_t)(m / 2) : 128;
       const size_t nkb = ((size_t)c_out + kb - 1) / kb;
       const size_t c16 = ((size_t)c_in + 15) / 16;
-      const size_t parts = (layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3) ? 2 : 1;
+      const size_t parts = (layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3 ||
+                            layout == CWGK_LAYOUT_TC2H_X3)
+                               ? 2
+                               : 1;
       const size_t sets = pair ? 2 : 1;
-      return nkb * sets * c16 * nf * parts * 4096;
+      return nkb * sets * c16 * nf * parts * rows * 32;
     }
     default: return 0;
   }
@@ -218,11 +230,11 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
   const int esz = (flags & CWG_BF16) ? 2 : 4;
   out->gemm_flops = 2.0 * (double)n * th * tw * c_out * c_in * td2;
   out->alg_bytes = (double)n * c_in * h * w * esz + (double)n * c_out * h * w * esz +
-                   (double)weight_bytes_for(c_in, c_out, mm, layout_of(path, mm, flags)) +
+                   (double)weight_bytes_for(c_in, c_out, mm, layout_of(path, mm, flags, c_out)) +
                    4.0 * c_out;
   if (path == CWG_PATH_TC) {
     cwgk_tc_cfg t;
-    cwgk_tc_get_cfg(tc_x3(mm, flags), tc_variant(flags), mm, &t);
+    cwgk_tc_get_cfg(tc_x3(mm, flags), tc_variant(flags, mm, c_out), mm, &t);
     out->mma_products = tc_x3(mm, flags) ? 3 : 1;
     out->tiles_per_cta = t.tiles;
     out->cout_per_cta = t.kb;
@@ -232,11 +244,11 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
     out->tmem_cols = t.tmem_cols;
     out->ctas = ((long long)n * th * tw + t.tiles - 1) / t.tiles * ((c_out + t.kb - 1) / t.kb) *
                 t.ctas_per_tile_block *
-                cwgk_tc_splits(n, c_in, c_out, h, w, mm, tc_variant(flags),
+                cwgk_tc_splits(n, c_in, c_out, h, w, mm, tc_variant(flags, mm, c_out),
                                (flags & CWG_BF16) != 0, !(flags & CWG_NO_SPLIT), num_sms());
     out->ctas_launched = out->ctas;
     out->order = CWG_ORDER_GRID;
-    if (n > 0 && cwgk_tc_plan(n, c_in, c_out, h, w, mm, tc_x3(mm, flags), tc_variant(flags),
+    if (n > 0 && cwgk_tc_plan(n, c_in, c_out, h, w, mm, tc_x3(mm, flags), tc_variant(flags, mm, c_out),
                               (flags & CWG_BF16) != 0, !(flags & CWG_NO_SPLIT), num_sms(),
                               &out->ctas_launched, &out->order) != 0) {
       out->ctas_launched = out->ctas;
@@ -263,7 +275,7 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
 size_t cwg_weight_bytes(int c_in, int c_out, int m, unsigned flags) {
   int mm = 0, path = 0;
   if (decide(c_in, c_out, m, flags, &mm, &path)) return 0;
-  return weight_bytes_for(c_in, c_out, mm, layout_of(path, mm, flags));
+  return weight_bytes_for(c_in, c_out, mm, layout_of(path, mm, flags, c_out));
 }
 
 static int weight_common(const float *src, void *U, int c_in, int c_out, int m, unsigned flags,
@@ -274,7 +286,7 @@ static int weight_common(const float *src, void *U, int c_in, int c_out, int m, 
   const int rc = decide(c_in, c_out, m, flags, &mm, &path);
   if (rc) return rc;
   if (from_ref && m == 0) return CWG_EINVAL; /* a reference-layout U fixes td */
-  return cwgk_weight_transform(src, U, c_in, c_out, mm, layout_of(path, mm, flags), from_ref,
+  return cwgk_weight_transform(src, U, c_in, c_out, mm, layout_of(path, mm, flags, c_out), from_ref,
                                stream);
 }
 
@@ -305,7 +317,7 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   const int bf16 = (flags & CWG_BF16) ? 1 : 0;
   if (path == CWG_PATH_TC) {
     return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, mm, tc_x3(mm, flags),
-                        tc_variant(flags), bf16, relu, !(flags & CWG_NO_SPLIT), stream);
+                        tc_variant(flags, mm, c_out), bf16, relu, !(flags & CWG_NO_SPLIT), stream);
   }
   cwgk_ffma_cfg cfg;
   const int idx = pick_ffma(n, c_out, h, w, mm, &cfg);

@@ -18,14 +18,17 @@ enum {
   CWGK_LAYOUT_TC_X3 = 3,     /* bf16 hi+lo UMMA blocks (fp32-parity tensor path)  */
   CWGK_LAYOUT_TC_X1 = 4,     /* bf16 UMMA blocks (single product)                 */
   CWGK_LAYOUT_TC2_X3 = 5,    /* pair kernel: At-scaled hi+lo blocks, 2 rank sets  */
-  CWGK_LAYOUT_TC2_X1 = 6     /* pair kernel: At-scaled blocks, single product     */
+  CWGK_LAYOUT_TC2_X1 = 6,    /* pair kernel: At-scaled blocks, single product     */
+  CWGK_LAYOUT_TC2H_X3 = 7,   /* 64-channel pair kernel: 64-row hi+lo blocks       */
+  CWGK_LAYOUT_TC2H_X1 = 8    /* 64-channel pair kernel: 64-row blocks, 1 product  */
 };
 
 /* Tensor-core kernel variants. */
 enum {
   CWGK_TC_PAIR = 0,   /* 2-SM pair, M = 256 (stacked output rows), F(2,3) and F(4,3) */
   CWGK_TC_HALF = 1,   /* one CTA, half-folded, M = 128, N = 64                  */
-  CWGK_TC_FULL16 = 2  /* one CTA, 16 frequency accumulators, N = 32             */
+  CWGK_TC_FULL16 = 2, /* one CTA, 16 frequency accumulators, N = 32             */
+  CWGK_TC_PAIR64 = 3  /* 2-SM pair, M = 128: 64 output channels, F(2,3) only     */
 };
 
 /* One compiled FFMA kernel configuration. */

@@ -766,11 +766,19 @@ __device__ __forceinline__ void ld_pair(const __nv_bfloat16 *p, bool ok, float &
 //           N = 128, 4 accumulators Z[r][b] x 128 columns.
 //   F(4,3): rank r holds 2 x 64 rows (i = 2r + il, output channel), 32 tiles
 //           of V; N = 64, 6 accumulators x 64 columns.
-template <int M>
+//   HM ("half M", F(2,3) layers of at most 64 output channels): M = 128, rank r
+//           holds 64 rows (i = r, output channel); in TMEM the accumulator's
+//           columns [0, N/2) sit in lanes 0-63 and [N/2, N) in lanes 64-127,
+//           both at columns 0 .. N/2-1.
+template <int M, bool HM = false>
 struct PairGeo {
+  static_assert(!HM || M == 2, "the M = 128 pair kernel is F(2,3) only");
   static constexpr int TD = M + 2, NF = TD * TD;
   static constexpr int kRowsI = M / 2;              // output rows i per CTA
-  static constexpr int kCoutCta = kCout / kRowsI;   // output channels per CTA
+  static constexpr int kRowsCta = HM ? 64 : kCout;  // A rows (MMA M / 2) per CTA
+  static constexpr int kMmaM = 2 * kRowsCta;        // MMA M of the pair
+  static constexpr int kCoutCta = kRowsCta / kRowsI;  // output channels per CTA
+  static constexpr int kBlkBytes = kRowsCta * kCc * 2;  // one weight block (rows x 16 ch)
   static constexpr int kTiles = M == 2 ? 64 : 32;   // V columns (tiles) per CTA
   static constexpr int kN = 2 * kTiles;             // MMA N of the pair
   static constexpr int kXWarps = 16;                // transform + epilogue warps
@@ -785,21 +793,22 @@ struct PairGeo {
   static constexpr int kGroups = M == 2 ? 1 : 2;
   static constexpr int kGroupWarps = kXWarps / kGroups;
   static constexpr int kCpt = 2;
-  static constexpr int kNU = 5;                     // weight stages
+  static constexpr int kNU = HM ? 8 : 5;            // weight stages
   static constexpr int kVBytes = kTiles * kCc * 2;  // one frequency of V
   static constexpr int kEpiTiles = 32 / M;          // tiles per 32-pixel epilogue patch row
   static_assert(TD * kN <= kTmemCols, "accumulators fit TMEM");
   static_assert(kTiles * kCc == kGroupWarps * 32 * kCpt, "one (tile, channels) per thread");
 };
 
-// Pair weight layout: [ceil(C_out/cout_cta)][rank = 2][C_pad/16][NF f][parts][4096 B]:
+// Pair weight layout: [ceil(C_out/cout_cta)][rank = 2][C_pad/16][NF f][parts][block]
+// (blocks of rows_cta rows x 16 channels: 4096 B, or 2048 B for HM):
 // block row il * cout_cta + k' of rank r holds At[r * rows_i + il][a] * U_ab for
 // output channel kblk * cout_cta + k' (scaling by 0, +-1, +-2, +-4, +-8 is exact
 // in bf16).  Channels past C_out / C_in are zero.
-template <int M, bool X3>
+template <int M, bool X3, bool HM>
 __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__restrict__ U,
                                      int C, int K, int Cp, int Kp, int from_ref) {
-  using G = PairGeo<M>;
+  using G = PairGeo<M, HM>;
   constexpr int NF = G::NF, TD = G::TD;
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)Cp * Kp) return;
@@ -824,23 +833,23 @@ __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__r
       for (int f = 0; f < NF; ++f) {
         const float s = Wino<M>::at(r * G::kRowsI + il, f / TD) * u[f];
         const __nv_bfloat16 hi = __float2bfloat16_rn(s);
-        uint8_t *b = U + ((blk0 * NF + f) * parts) * kCoreBytes;
+        uint8_t *b = U + ((blk0 * NF + f) * parts) * G::kBlkBytes;
         *reinterpret_cast<__nv_bfloat16 *>(b + off) = hi;
         if (X3)
-          *reinterpret_cast<__nv_bfloat16 *>(b + kCoreBytes + off) =
+          *reinterpret_cast<__nv_bfloat16 *>(b + G::kBlkBytes + off) =
               __float2bfloat16_rn(s - __bfloat162float(hi));
       }
     }
 }
 
 // Shared memory of one CTA of the pair.
-template <int M, bool X3>
+template <int M, bool X3, bool HM = false>
 struct PairLayout {
-  using G = PairGeo<M>;
+  using G = PairGeo<M, HM>;
   static constexpr int kNU = G::kNU;
   static constexpr int kParts = X3 ? 2 : 1;
   static constexpr int kVStage = kParts * G::NF * G::kVBytes;
-  static constexpr int kUStage = kFPerU * kParts * kCoreBytes;
+  static constexpr int kUStage = kFPerU * kParts * G::kBlkBytes;
   static constexpr int kVOff = 0;
   static constexpr int kUOff = kVOff + kNV * kVStage;
   static constexpr int kBarOff = kUOff + kNU * kUStage;
@@ -921,14 +930,14 @@ constexpr int kBarEpi = 2;
 // abort (then only its barrier arrivals), so that the named barriers match.  Not
 // inlined: its registers stay out of the transform loop, which calls it once per
 // item.
-template <int M, bool X3, typename Tio>
+template <int M, bool X3, typename Tio, bool HM>
 __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *smem,
                                            const float *__restrict__ bias, Tio *__restrict__ y,
                                            int K, int H, int W, int tiles_y, int tiles_x,
                                            int total_tiles, int chunk, int kb_count,
                                            int relu, int split) {
-  using L = PairLayout<M, X3>;
-  using G = PairGeo<M>;
+  using L = PairLayout<M, X3, HM>;
+  using G = PairGeo<M, HM>;
   constexpr int TD = G::TD, kN = G::kN, kNU = L::kNU;
   constexpr int kEpiThreads = 32 * G::kXWarps;
   const uint32_t sbase = smem_u32(smem);
@@ -947,7 +956,9 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
   // the item and its bias load before the wait for the accumulators
   const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, e);
   const int quad = warp & 3;
-  const int kq = it.kb * G::kCoutCta + (quad * 32) % G::kCoutCta;
+  // TMEM lanes 32 quad .. 32 quad + 31: channels kq .. kq + 31 of output row
+  // irow; HM: lanes 64-127 repeat channels 0-63 for the second half of the columns
+  const int kq = it.kb * G::kCoutCta + (HM ? 32 * (quad & 1) : (quad * 32) % G::kCoutCta);
   // a split adds its partial sums into y (zeroed by the host); slice 0 adds
   // the bias unless a ReLU must follow the full sum, in which case a separate
   // pass applies both once every slice has landed
@@ -958,9 +969,17 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
   if (run) {
     constexpr int kE = G::kEpiTiles;
     const uint32_t tmem = *tmem_slot;
-    const int il = (quad * 32) / G::kCoutCta;
+    const int il = HM ? 0 : (quad * 32) / G::kCoutCta;
     const int irow = (int)rank * G::kRowsI + il;  // output row i of the tile
-    const int col0 = (tw >> 2) * (kN / 4);        // 32 (F2) or 16 (F4) columns per warp
+    // item columns [col0, lim) of this warp, at TMEM column (column - tshift):
+    // 32 (F2) or 16 (F4) per warp; HM: 16 per warp within its lanes' half
+    int col0 = (tw >> 2) * (kN / 4), lim = it.cnt, tshift = 0;
+    if constexpr (HM) {
+      const int nh = item_n(it.cnt) >> 1, hq = quad >> 1;
+      tshift = hq * nh;
+      col0 = tshift + (tw >> 2) * kE;
+      lim = it.cnt < tshift + nh ? it.cnt : tshift + nh;
+    }
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     const int pslot = ((e + 1) * nst + 1) % kNV;
     float *patch =
@@ -970,15 +989,16 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
     const bool do_relu = relu && !split;
     const int kmax = K - kq < 32 ? K - kq : 32;
 #pragma unroll 1
-    for (int gq = 0; gq < (kN / 4) / kE; ++gq) {
+    for (int gq = 0; gq < (HM ? 1 : (kN / 4) / kE); ++gq) {
       const int cb = col0 + gq * kE;
-      if (cb >= it.cnt) break;
+      if (cb >= lim) break;
       // 8 tiles (columns) at a time from TMEM: TD x 8 registers
 #pragma unroll 1
       for (int h = 0; h < kE; h += 8) {
         float z[TD][8];
 #pragma unroll
-        for (int b = 0; b < TD; ++b) tmem_ld8(trow + (uint32_t)(b * kN + cb + h), z[b]);
+        for (int b = 0; b < TD; ++b)
+          tmem_ld8(trow + (uint32_t)(b * kN + cb - tshift + h), z[b]);
         tmem_wait_ld();
 #pragma unroll
         for (int q = 0; q < 2 * M; ++q) {  // 4 pixels (px = 4q ..) of this 8-tile half
@@ -1014,7 +1034,7 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
       for (int u = 0; u < 4 / M; ++u) {
         const int tt = cb + (4 * q) / M + u;  // column = tile of the item
         long long o = -1;
-        if (tt < it.cnt) {
+        if (tt < lim) {
           const int TT = it.t0 + tt;
           const int nn = TT / per_img;
           const int rem = TT - nn * per_img;
@@ -1049,7 +1069,7 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
         }
       } else {
         const int tt = cb + lane / M, j = lane % M;  // lane = pixel
-        if (tt < it.cnt) {
+        if (tt < lim) {
           const int TT = it.t0 + tt;
           const int nn = TT / per_img;
           const int rem = TT - nn * per_img;
@@ -1093,14 +1113,14 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
   return run;
 }
 
-template <int M, bool X3, typename Tio>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads, 1)
+template <int M, bool X3, typename Tio, bool HM>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThreads, 1)
     wino_fused_tc_pair(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                        const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
                        int W, int tiles_y, int tiles_x, int total_tiles, int relu,
                        int cs_per_split, int split, int chunk, int kb_count) {
-  using L = PairLayout<M, X3>;
-  using G = PairGeo<M>;
+  using L = PairLayout<M, X3, HM>;
+  using G = PairGeo<M, HM>;
   constexpr int P = L::kParts, TD = G::TD, NF = G::NF;
   constexpr int kTiles = G::kTiles, kN = G::kN, kNU = L::kNU, kVBytes = G::kVBytes;
   constexpr int kXW = G::kXWarps;
@@ -1175,7 +1195,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
       int ui = 0, g = 0;
       for (int j = 0; ok && j < n_items; ++j) {
         const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
-        const uint32_t idesc = instr_desc(2 * kCout, item_n(it.cnt));
+        const uint32_t idesc = instr_desc(G::kMmaM, item_n(it.cnt));
         if (j > 0) {
           // both CTAs' epilogue warps have read item j-1's accumulators
           ok = __all_sync(0xffffffffu, mbar_wait(tmem_empty, (j - 1) & 1, abort));
@@ -1201,7 +1221,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
 #pragma unroll
             for (int fi = 0; fi < kFPerU; ++fi) {
               const int f = fp * kFPerU + fi;
-              const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * kCoreBytes) >> 4);
+              const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * G::kBlkBytes) >> 4);
               const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
               // accumulator Z[.][b], b = f % TD; its first term is a = 0 of stage 0
               const uint32_t d = tmem + (uint32_t)((f % TD) * kN);
@@ -1210,7 +1230,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
               if (X3) {
                 if (elect_one()) mma_pair_bf16(d, ah, bh + kLo, idesc, 1u);
                 if (elect_one())
-                  mma_pair_bf16(d, ah + (uint64_t)(kCoreBytes >> 4), bh, idesc, 1u);
+                  mma_pair_bf16(d, ah + (uint64_t)(G::kBlkBytes >> 4), bh, idesc, 1u);
               }
             }
             __syncwarp();
@@ -1262,7 +1282,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     bool ok = true;
     for (int j = 0; ok && j < n_items; ++j) {
       const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
-      const uint8_t *ublk = U + ((size_t)it.kb * 2 + rank) * C16 * NF * P * kCoreBytes +
+      const uint8_t *ublk = U + ((size_t)it.kb * 2 + rank) * C16 * NF * P * G::kBlkBytes +
                             (size_t)cs0 * kUPerStage * L::kUStage;
       for (int q = 0; q < nst * kUPerStage; ++q) {
         const int s = issued % kNU;
@@ -1404,7 +1424,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
     for (int s = grp; s < S; s += G::kGroups) {
       if (ep < n_items && s > (ep + 1) * nst) {
         do {
-          ok = pair_epilogue<M, X3, Tio>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
+          ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
                                          tiles_x, total_tiles, chunk, kb_count, relu, split) &&
                ok;
         } while (ep < n_items && s > (ep + 1) * nst);
@@ -1478,7 +1498,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M>::kThreads
         if (sn < S && !(ep < n_items && sn > (ep + 1) * nst)) load_stage(sn);
       }
     }
-    while (ep < n_items) ok = pair_epilogue<M, X3, Tio>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
+    while (ep < n_items) ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
                                            total_tiles, chunk, kb_count, relu, split) && ok;
     if (n_items == 0) named_bar_sync(kBarTmem, 32 + kEpiThreads);
   }
@@ -1510,9 +1530,9 @@ __global__ void bias_relu_pass(float *__restrict__ y, const float *__restrict__ 
 // idle: each slice keeps at least 2 stages.  1 = no split.  (Above that occupancy
 // the extra zeroing, atomics and bias pass cost more than the shorter C_in loop
 // saves.)
-template <int M>
+template <int M, bool HM>
 static int split_stages(int n, int c, int k, int h, int w, int tpcs, int *per) {
-  using G = PairGeo<M>;
+  using G = PairGeo<M, HM>;
   const int C16 = (c + kCc - 1) / kCc;
   const long long tiles = (long long)n * ((h + M - 1) / M) * ((w + M - 1) / M);
   const long long items = (tiles + G::kN - 1) / G::kN * ((k + G::kCoutCta - 1) / G::kCoutCta);
@@ -1559,9 +1579,9 @@ struct PairPlan {
   int gy, kb_count;
   int order;  // CWG_ORDER_*
 };
-template <int M>
+template <int M, bool HM>
 static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
-  using G = PairGeo<M>;
+  using G = PairGeo<M, HM>;
   constexpr double kFixed = M == 2 ? 0.5 : 0.75, kPrologue = 0.1;
   const long long blocks = (total + G::kN - 1) / G::kN, units = blocks * gy;
   PairPlan p{blocks, G::kN, gy, 1, CWG_ORDER_GRID};
@@ -1592,12 +1612,12 @@ static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
   return p;
 }
 
-template <int M, bool X3, typename Tio>
+template <int M, bool X3, typename Tio, bool HM>
 static cudaError_t launch_pair(const void *x, const void *U, const float *bias, void *y, int n,
                                int c, int k, int h, int w, int relu, int allow_split,
                                cudaStream_t s) {
-  using G = PairGeo<M>;
-  using L = PairLayout<M, X3>;
+  using G = PairGeo<M, HM>;
+  using L = PairLayout<M, X3, HM>;
   const int tiles_y = (h + M - 1) / M, tiles_x = (w + M - 1) / M;
   const long long total = (long long)n * tiles_y * tiles_x;
   const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
@@ -1606,14 +1626,14 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   int per = (c + kCc - 1) / kCc;
-  const int splits = (allow_split && sizeof(Tio) == 4) ? split_stages<M>(n, c, k, h, w, sms / 2,
+  const int splits = (allow_split && sizeof(Tio) == 4) ? split_stages<M, HM>(n, c, k, h, w, sms / 2,
                                                                          &per)
                                                        : 1;
-  auto fn = wino_fused_tc_pair<M, X3, Tio>;
-  e = smem_attr_once<wino_fused_tc_pair<M, X3, Tio>>(L::kSmem);
+  auto fn = wino_fused_tc_pair<M, X3, Tio, HM>;
+  e = smem_attr_once<wino_fused_tc_pair<M, X3, Tio, HM>>(L::kSmem);
   if (e != cudaSuccess) return e;
-  const int resident = resident_pairs<wino_fused_tc_pair<M, X3, Tio>>(G::kThreads, L::kSmem, sms);
-  const PairPlan plan = plan_pairs<M>(total, gy, splits, resident);
+  const int resident = resident_pairs<wino_fused_tc_pair<M, X3, Tio, HM>>(G::kThreads, L::kSmem, sms);
+  const PairPlan plan = plan_pairs<M, HM>(total, gy, splits, resident);
   // tile indices, item counts and units are 32-bit in the kernel
   if (total * gy > 0x7fffffffLL || 2 * plan.pairs > 0x7fffffffLL || plan.gy > 65535)
     return cudaErrorInvalidValue;
@@ -1636,23 +1656,23 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
 
 // The launch plan of a layer as launch_pair would make it on the current device
 // (without one: `sms` SMs and one cluster per TPC).
-template <int M, bool X3, typename Tio>
+template <int M, bool X3, typename Tio, bool HM>
 static void plan_layer(int n, int c, int k, int h, int w, int allow_split, int sms,
                        long long *ctas, int *order) {
-  using G = PairGeo<M>;
-  using L = PairLayout<M, X3>;
+  using G = PairGeo<M, HM>;
+  using L = PairLayout<M, X3, HM>;
   const long long total = (long long)n * ((h + M - 1) / M) * ((w + M - 1) / M);
   const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
   int per = 0;
   const int splits =
-      (allow_split && sizeof(Tio) == 4) ? split_stages<M>(n, c, k, h, w, sms / 2, &per) : 1;
+      (allow_split && sizeof(Tio) == 4) ? split_stages<M, HM>(n, c, k, h, w, sms / 2, &per) : 1;
   int resident = sms / 2, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess &&
-      smem_attr_once<wino_fused_tc_pair<M, X3, Tio>>(L::kSmem) == cudaSuccess)
-    resident = resident_pairs<wino_fused_tc_pair<M, X3, Tio>>(G::kThreads, L::kSmem, sms);
+      smem_attr_once<wino_fused_tc_pair<M, X3, Tio, HM>>(L::kSmem) == cudaSuccess)
+    resident = resident_pairs<wino_fused_tc_pair<M, X3, Tio, HM>>(G::kThreads, L::kSmem, sms);
   else
     (void)cudaGetLastError();
-  const PairPlan p = plan_pairs<M>(total, gy, splits, resident);
+  const PairPlan p = plan_pairs<M, HM>(total, gy, splits, resident);
   *ctas = 2 * p.pairs * p.gy * splits;
   *order = p.order;
 }
@@ -1703,6 +1723,15 @@ int cwgk_tc_get_cfg(int x3, int variant, int m, cwgk_tc_cfg *out) {
     out->ctas_per_tile_block = 2;
     return 0;
   }
+  if (variant == CWGK_TC_PAIR64) {
+    if (m != 2) return -1;
+    out->tiles = tc::PairGeo<2, true>::kN;
+    out->kb = tc::PairGeo<2, true>::kCoutCta;
+    out->threads = tc::PairGeo<2, true>::kThreads;
+    out->smem = x3 ? tc::PairLayout<2, true, true>::kSmem : tc::PairLayout<2, false, true>::kSmem;
+    out->ctas_per_tile_block = 2;
+    return 0;
+  }
   if (m != 2) return -1;
   switch (variant) {
     case CWGK_TC_HALF:
@@ -1723,11 +1752,15 @@ int cwgk_tc_get_cfg(int x3, int variant, int m, cwgk_tc_cfg *out) {
 
 int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int m, int layout,
                              int from_ref, void *stream) {
-  const bool pair = layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
-  const bool x3 = layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3;
-  if (!(m == 2 || (m == 4 && pair))) return -2;
+  const bool half = layout == CWGK_LAYOUT_TC2H_X3 || layout == CWGK_LAYOUT_TC2H_X1;
+  const bool pair = half || layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
+  const bool x3 = layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3 ||
+                  layout == CWGK_LAYOUT_TC2H_X3;
+  if (!(m == 2 || (m == 4 && pair && !half))) return -2;
   if (!pair && layout != CWGK_LAYOUT_TC_X1 && layout != CWGK_LAYOUT_TC_X3) return -2;
-  const int kb = pair ? (m == 2 ? tc::PairGeo<2>::kCoutCta : tc::PairGeo<4>::kCoutCta) : tc::kCout;
+  const int kb = half ? tc::PairGeo<2, true>::kCoutCta
+                      : (pair ? (m == 2 ? tc::PairGeo<2>::kCoutCta : tc::PairGeo<4>::kCoutCta)
+                              : tc::kCout);
   const int Cp = (c_in + tc::kCc - 1) / tc::kCc * tc::kCc;
   const int Kp = (c_out + kb - 1) / kb * kb;
   const long total = (long)Cp * Kp;
@@ -1741,16 +1774,21 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
       CWG_WT(tc::wt_transform_tc<true>);
     else
       CWG_WT(tc::wt_transform_tc<false>);
+  } else if (half) {
+    if (x3)
+      CWG_WT((tc::wt_transform_tc_pair<2, true, true>));
+    else
+      CWG_WT((tc::wt_transform_tc_pair<2, false, true>));
   } else if (m == 2) {
     if (x3)
-      CWG_WT((tc::wt_transform_tc_pair<2, true>));
+      CWG_WT((tc::wt_transform_tc_pair<2, true, false>));
     else
-      CWG_WT((tc::wt_transform_tc_pair<2, false>));
+      CWG_WT((tc::wt_transform_tc_pair<2, false, false>));
   } else {
     if (x3)
-      CWG_WT((tc::wt_transform_tc_pair<4, true>));
+      CWG_WT((tc::wt_transform_tc_pair<4, true, false>));
     else
-      CWG_WT((tc::wt_transform_tc_pair<4, false>));
+      CWG_WT((tc::wt_transform_tc_pair<4, false, false>));
   }
 #undef CWG_WT
   cwgk_count_launch();
@@ -1765,26 +1803,34 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
 int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant, int bf16,
                    int allow_split, int sms) {
   int per = 0;
-  if (variant != CWGK_TC_PAIR || bf16 || !allow_split) return 1;
-  return m == 2 ? tc::split_stages<2>(n, c_in, c_out, h, w, sms / 2, &per)
-                : tc::split_stages<4>(n, c_in, c_out, h, w, sms / 2, &per);
+  if ((variant != CWGK_TC_PAIR && variant != CWGK_TC_PAIR64) || bf16 || !allow_split) return 1;
+  if (variant == CWGK_TC_PAIR64)
+    return m == 2 ? tc::split_stages<2, true>(n, c_in, c_out, h, w, sms / 2, &per) : 1;
+  return m == 2 ? tc::split_stages<2, false>(n, c_in, c_out, h, w, sms / 2, &per)
+                : tc::split_stages<4, false>(n, c_in, c_out, h, w, sms / 2, &per);
 }
 
 int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int x3, int variant, int bf16,
                  int allow_split, int sms, long long *ctas, int *order) {
-  if (variant != CWGK_TC_PAIR || !(m == 2 || m == 4)) return -1;
-#define CWG_PLAN(M_, X3_, T_) \
-  tc::plan_layer<M_, X3_, T_>(n, c_in, c_out, h, w, allow_split, sms, ctas, order)
-  if (m == 2) {
+  if (!(variant == CWGK_TC_PAIR && (m == 2 || m == 4)) && !(variant == CWGK_TC_PAIR64 && m == 2))
+    return -1;
+#define CWG_PLAN(M_, X3_, T_, HM_) \
+  tc::plan_layer<M_, X3_, T_, HM_>(n, c_in, c_out, h, w, allow_split, sms, ctas, order)
+  if (variant == CWGK_TC_PAIR64) {
     if (bf16)
-      x3 ? CWG_PLAN(2, true, __nv_bfloat16) : CWG_PLAN(2, false, __nv_bfloat16);
+      x3 ? CWG_PLAN(2, true, __nv_bfloat16, true) : CWG_PLAN(2, false, __nv_bfloat16, true);
     else
-      x3 ? CWG_PLAN(2, true, float) : CWG_PLAN(2, false, float);
+      x3 ? CWG_PLAN(2, true, float, true) : CWG_PLAN(2, false, float, true);
+  } else if (m == 2) {
+    if (bf16)
+      x3 ? CWG_PLAN(2, true, __nv_bfloat16, false) : CWG_PLAN(2, false, __nv_bfloat16, false);
+    else
+      x3 ? CWG_PLAN(2, true, float, false) : CWG_PLAN(2, false, float, false);
   } else {
     if (bf16)
-      x3 ? CWG_PLAN(4, true, __nv_bfloat16) : CWG_PLAN(4, false, __nv_bfloat16);
+      x3 ? CWG_PLAN(4, true, __nv_bfloat16, false) : CWG_PLAN(4, false, __nv_bfloat16, false);
     else
-      x3 ? CWG_PLAN(4, true, float) : CWG_PLAN(4, false, float);
+      x3 ? CWG_PLAN(4, true, float, false) : CWG_PLAN(4, false, float, false);
   }
 #undef CWG_PLAN
   return 0;
@@ -1798,15 +1844,17 @@ int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n
 #define CWG_TC_LAUNCH(X3_, HALF_)                                                              \
   (bf16 ? tc::launch<X3_, HALF_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s) \
         : tc::launch<X3_, HALF_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
-#define CWG_TC_LAUNCH_PAIR(M_, X3_)                                                             \
-  (bf16 ? tc::launch_pair<M_, X3_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu,  \
-                                                   allow_split, s)                             \
-        : tc::launch_pair<M_, X3_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu,          \
-                                          allow_split, s))
+#define CWG_TC_LAUNCH_PAIR(M_, X3_, HM_)                                                        \
+  (bf16 ? tc::launch_pair<M_, X3_, __nv_bfloat16, HM_>(x, U, bias, y, n, c_in, c_out, h, w,   \
+                                                        relu, allow_split, s)                 \
+        : tc::launch_pair<M_, X3_, float, HM_>(x, U, bias, y, n, c_in, c_out, h, w, relu,     \
+                                               allow_split, s))
   if (variant == CWGK_TC_PAIR && m == 2)
-    e = x3 ? CWG_TC_LAUNCH_PAIR(2, true) : CWG_TC_LAUNCH_PAIR(2, false);
+    e = x3 ? CWG_TC_LAUNCH_PAIR(2, true, false) : CWG_TC_LAUNCH_PAIR(2, false, false);
+  else if (variant == CWGK_TC_PAIR64 && m == 2)
+    e = x3 ? CWG_TC_LAUNCH_PAIR(2, true, true) : CWG_TC_LAUNCH_PAIR(2, false, true);
   else if (variant == CWGK_TC_PAIR && m == 4)
-    e = x3 ? CWG_TC_LAUNCH_PAIR(4, true) : CWG_TC_LAUNCH_PAIR(4, false);
+    e = x3 ? CWG_TC_LAUNCH_PAIR(4, true, false) : CWG_TC_LAUNCH_PAIR(4, false, false);
   else if (variant == CWGK_TC_HALF && m == 2)
     e = x3 ? CWG_TC_LAUNCH(true, true) : CWG_TC_LAUNCH(false, true);
   else if (variant == CWGK_TC_FULL16 && m == 2)

@@ -129,6 +129,23 @@ def test_selector_tensor_core_variants():
     assert e.value.status == cwg.EINVAL
 
 
+def test_selector_64_channel_pair():
+    """F(2,3) layers of at most 64 output channels run the pair kernel with M = 128:
+    64 channels per CTA and 64-row weight blocks (2048 bytes)."""
+    c, k = 96, 64
+    ch = cwg.select(4, c, k, 56, 56, 2, cwg.NO_SPLIT)
+    assert ch.path == cwg.PATH_TC and ch.cout_per_cta == 64 and ch.tiles_per_cta == 128
+    # [1 channel block][2 ranks][6 C_in steps][16 f][hi, lo] blocks of 64 x 16 bf16
+    assert cwg.weight_bytes(c, k, 2) == 1 * 2 * 6 * 16 * 2 * 2048
+    assert cwg.weight_bytes(c, k, 2, cwg.BF16) == 1 * 2 * 6 * 16 * 1 * 2048
+    # 65 channels and up: the M = 256 kernel, 128 channels per CTA
+    assert cwg.select(4, c, 65, 56, 56).cout_per_cta == 128
+    assert cwg.weight_bytes(c, 65, 2) == 1 * 2 * 6 * 16 * 2 * 4096
+    # F(4,3) and the single-CTA ablations keep their layouts
+    assert cwg.select(4, c, k, 56, 56, 4, cwg.BF16).cout_per_cta == 64
+    assert cwg.select(4, c, k, 56, 56, 2, cwg.TC_NOPAIR).cout_per_cta == 128
+
+
 def test_selector_launch_plan():
     """Which grid the pair kernel launches (without a device: 74 TPCs, one cluster each)."""
     small = cwg.select(4, 128, 128, 56, 56)  # 25 tile blocks: one per CTA pair

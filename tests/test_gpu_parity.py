@@ -341,6 +341,7 @@ PERSISTENT = [
     # n, c, k, h, w, m, flags
     (13, 64, 136, 56, 56, 2, 0),                    # fp32 F(2,3), 2 ragged channel blocks
     (13, 64, 64, 56, 56, 2, cwg.BF16),               # bf16 F(2,3): patches outside the V ring
+    (13, 96, 64, 56, 56, 2, 0),                      # fp32 F(2,3), 64 channels: M = 128 pair
     (25, 64, 72, 56, 56, 4, cwg.BF16),               # bf16 F(4,3), 2 ragged channel blocks
 ]
 
@@ -364,7 +365,8 @@ def test_persistent_pairs(cuda_dev, case):
 
 @pytest.mark.parametrize("case", [
     (128, 200, 2, 0), (128, 200, 2, cwg.BF16), (128, 200, 2, cwg.TC_NOPAIR),
-    (128, 200, 2, cwg.TC_FULL16), (96, 200, 4, cwg.BF16), (32, 40, 2, 0), (32, 40, 4, cwg.BF16)],
+    (128, 200, 2, cwg.TC_FULL16), (96, 200, 4, cwg.BF16), (32, 40, 2, 0), (32, 40, 4, cwg.BF16),
+    (80, 64, 2, 0), (80, 64, 2, cwg.BF16)],  # the 64-channel pair kernel's 64-row blocks
     ids=lambda c: f"c{c[0]}k{c[1]}m{c[2]}f{c[3]:#x}")
 def test_weight_transform_stays_in_its_buffer(cuda_dev, case):
     """Every weight layout is written exactly inside cwg_weight_bytes: guard
