@@ -1422,16 +1422,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       if (grp < S) load_stage(grp);
     }
     for (int s = grp; s < S; s += G::kGroups) {
-      if (ep < n_items && s > (ep + 1) * nst) {
-        do {
-          ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
-                                         tiles_x, total_tiles, chunk, kb_count, relu, split) &&
-               ok;
-        } while (ep < n_items && s > (ep + 1) * nst);
-        // F(2,3): this stage's patches were not loaded ahead of the epilogue (their
-        // loads would have queued in front of its stores)
-        if constexpr (M == 2) load_stage(s);
-      }
+      // (F(2,3): stage s's patches are already in registers, their loads having
+      // overlapped the last MMAs and the epilogue)
+      while (ep < n_items && s > (ep + 1) * nst)
+        ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
+                                           tiles_x, total_tiles, chunk, kb_count, relu, split) &&
+             ok;
       if (!ok) break;
       const int vs = s % kNV;
       if constexpr (M != 2) load_stage(s);
@@ -1495,7 +1491,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       if (lane == 0) mbar_arrive(v_full + 8 * vs);
       if constexpr (M == 2) {
         const int sn = s + G::kGroups;
-        if (sn < S && !(ep < n_items && sn > (ep + 1) * nst)) load_stage(sn);
+        if (sn < S) load_stage(sn);
       }
     }
     while (ep < n_items) ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
