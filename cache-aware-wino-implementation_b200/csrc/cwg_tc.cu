@@ -925,11 +925,12 @@ constexpr int kBarEpi = 2;
 
 // Epilogue of item e of a pair, run by every transform warp: output rows M ty + i
 // of the item's tiles.  TMEM lane = (il, output channel).  Each group of
-// kEpiTiles tiles (32 output pixels of one row) goes through the warp's patch so
-// that a warp store writes one 128-byte row segment of one channel plane.  Every warp runs every item's epilogue, also after an
-// abort (then only its barrier arrivals), so that the named barriers match.  Not
-// inlined: its registers stay out of the transform loop, which calls it once per
-// item.
+// kEpiTiles tiles (32 output pixels of one row) goes through the warp's 32 x 32
+// patch, then out as 16-byte stores of 4 pixels of one channel (or, at image
+// edges and odd alignments, one channel plane per warp store).  Every warp runs
+// every item's epilogue, also after an abort (then only its barrier arrivals), so
+// that the named barriers match.  Not inlined: its registers stay out of the
+// transform loop, which calls it once per item.
 template <int M, bool X3, typename Tio, bool HM>
 __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *smem,
                                            const float *__restrict__ bias, Tio *__restrict__ y,
