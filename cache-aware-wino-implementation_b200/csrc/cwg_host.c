@@ -187,16 +187,34 @@ static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
 
 /* Picks the FFMA configuration for a layer (index into the shim's table):
  * the widest output-channel block that still gives at least one CTA per SM. */
-static int find_ffma(int m, int kb, cwgk_ffma_cfg *c) {
+static int find_ffma_ty(int m, int kb, int ty, cwgk_ffma_cfg *c) {
   const int ncfg = cwgk_ffma_num_cfgs();
   for (int i = 0; i < ncfg; ++i)
-    if (cwgk_ffma_get_cfg(i, c) == 0 && c->m == m && c->kb == kb && c->ty == 4) return i;
+    if (cwgk_ffma_get_cfg(i, c) == 0 && c->m == m && c->kb == kb && c->ty == ty) return i;
   return -1;
 }
+static int find_ffma(int m, int kb, cwgk_ffma_cfg *c) { return find_ffma_ty(m, kb, 4, c); }
 
 static int pick_ffma(int n, int c_out, int h, int w, int m, cwgk_ffma_cfg *cfg_out) {
   const int sms = num_sms();
   const long long th = (h + m - 1) / m, tw = (w + m - 1) / m;
+  /* Large images first try 8x8-tile blocks of 32 channels: a CTA's weight
+   * chunk then serves 64 tiles instead of 16, and the grid has a quarter of
+   * the CTAs, each of which pays its load / transform / store latency once
+   * (a 3->64 layer at 224x224, 32 images: 521 vs 791 us).  Only when that grid
+   * still fills every SM. */
+  if (c_out >= 32) {
+    cwgk_ffma_cfg c;
+    const int idx = find_ffma_ty(m, 32, 8, &c);
+    if (idx >= 0) {
+      const long long ctas = (long long)n * ((th + c.ty - 1) / c.ty) * ((tw + c.tx - 1) / c.tx) *
+                             ((c_out + c.kb - 1) / c.kb);
+      if (ctas >= sms) {
+        if (cfg_out) *cfg_out = c;
+        return idx;
+      }
+    }
+  }
   int kb = c_out >= 64 ? 64 : (c_out > 16 ? 32 : 16);
   for (;;) {
     cwgk_ffma_cfg c;
