@@ -136,7 +136,7 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
    * F(2,3); take it for bf16 data, whose rounding already dominates the error,
    * and keep F(2,3) (the reference's default, src/cache_adaptive_autotiler.py:70-73)
    * for fp32. */
-  *m_out = m ? m : ((flags & CWG_BF16) ? 4 : 2);
+  *m_out = m ? m : ((flags & CWG_BF16) && c_in > 4 ? 4 : 2);  /* 1-4 channels: own F(2,3) kernel */
   *path_out = CWG_PATH_FFMA;
   return CWG_OK;
 }
@@ -194,6 +194,11 @@ static int find_ffma_ty(int m, int kb, int ty, cwgk_ffma_cfg *c) {
   return -1;
 }
 static int find_ffma(int m, int kb, cwgk_ffma_cfg *c) { return find_ffma_ty(m, kb, 4, c); }
+
+/* F(2,3) layers of 1-4 input channels (an RGB input layer) run the one-tile-per-
+ * thread kernel: they are bound by writing the output planes, and the general
+ * kernel's per-CTA staging of 8-channel weight chunks costs more than the math. */
+static int small_cin(int c_in, int m) { return m == 2 && c_in <= 4; }
 
 static int pick_ffma(int n, int c_out, int h, int w, int m, cwgk_ffma_cfg *cfg_out) {
   const int sms = num_sms();
@@ -272,6 +277,19 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
       out->ctas_launched = out->ctas;
       out->order = CWG_ORDER_GRID;
     }
+  } else if (small_cin(c_in, mm)) {
+    const long long gx = ((long long)n * th * tw + 255) / 256;
+    int kc = 64; /* the launch's rule: halve while the grid leaves SMs idle */
+    while (kc > 8 && gx * ((c_out + kc - 1) / kc) < 2LL * num_sms()) kc /= 2;
+    out->tiles_per_cta = 256; /* one thread per tile */
+    out->cout_per_cta = kc;
+    out->cin_chunk = c_in;
+    out->threads = 256;
+    out->smem_bytes = 64 * 16 * c_in * 4;
+    out->tmem_cols = 0;
+    out->ctas = gx * ((c_out + kc - 1) / kc);
+    out->ctas_launched = out->ctas;
+    out->order = CWG_ORDER_GRID;
   } else {
     cwgk_ffma_cfg c;
     if (pick_ffma(n, c_out, h, w, mm, &c) < 0) return CWG_EUNSUPPORTED;
@@ -337,6 +355,8 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
     return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, mm, tc_x3(mm, flags),
                         tc_variant(flags, mm, c_out), bf16, relu, !(flags & CWG_NO_SPLIT), stream);
   }
+  if (small_cin(c_in, mm))
+    return cwgk_conv_small(x, U, bias, y, n, c_in, c_out, h, w, bf16, relu, stream);
   cwgk_ffma_cfg cfg;
   const int idx = pick_ffma(n, c_out, h, w, mm, &cfg);
   if (idx < 0) return CWG_EUNSUPPORTED;

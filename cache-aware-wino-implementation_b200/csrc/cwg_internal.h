@@ -66,6 +66,11 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
                              int from_ref, void *stream);
 
 /* FFMA fused convolution with configuration `cfg_idx`. */
+/* F(2,3) for layers of 1-4 input channels (csrc/cwg_small.cu): one thread per tile,
+ * 64 output channels per CTA, weights in the CUDA-core layout. */
+int cwgk_conv_small(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
+                    int c_out, int h, int w, int bf16, int relu, void *stream);
+
 int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
                    int c_in, int c_out, int h, int w, int bf16, int relu, void *stream);
 

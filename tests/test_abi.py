@@ -63,6 +63,9 @@ def test_selector_auto_m_and_bf16():
     assert cwg.select(1, 16, 32, 56, 56, 0, cwg.BF16 | cwg.FORCE_FFMA).m == 4
     assert cwg.select(1, 16, 32, 56, 56, 4).m == 4
     assert cwg.select(1, 16, 32, 56, 56, 2).m == 2
+    # 1-4 input channels: F(2,3) on the one-tile-per-thread kernel, bf16 too
+    small = cwg.select(1, 3, 64, 224, 224, 0, cwg.BF16)
+    assert small.m == 2 and small.path == cwg.PATH_FFMA and small.threads == 256
 
 
 def test_selector_grid_covers_layer():

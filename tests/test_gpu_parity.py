@@ -363,6 +363,38 @@ def test_persistent_pairs(cuda_dev, case):
     assert_close(y, ref, "bf16" if bf else "f23", f"persistent {case}")
 
 
+# F(2,3) layers of 1-4 input channels (an RGB input layer) run their own kernel:
+# one thread per tile, 8-64 output channels per CTA.
+SMALL_CIN = [
+    # n, c, k, h, w, flags, bias
+    (2, 3, 64, 56, 56, 0, True),      # even width: pair loads, 2-pixel row stores
+    (1, 3, 200, 17, 23, 0, True),     # odd sizes: scalar path, ragged channel block
+    (3, 2, 40, 30, 31, 0, False),     # odd width, no bias
+    (1, 4, 72, 20, 20, 0, True),      # four channels
+    (1, 1, 16, 9, 10, 0, True),       # one channel
+    (2, 3, 64, 28, 28, cwg.BF16, True),
+]
+
+
+@pytest.mark.parametrize("case", SMALL_CIN, ids=lambda c: "x".join(map(str, c[:5])) + f"f{c[5]:#x}")
+def test_small_cin_layers(cuda_dev, case):
+    n, c, k, h, w, extra, use_bias = case
+    rng = np.random.default_rng(sum(case[:5]) + 1300)
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32) if use_bias else None
+    flags = cwg.RELU | extra
+    ch = cwg.select(n, c, k, h, w, 0, flags)
+    assert ch.path == cwg.PATH_FFMA and ch.m == 2 and ch.threads == 256
+    if extra & cwg.BF16:
+        x, g = workloads.bf16_round(x), workloads.bf16_round(g)
+        y = gpu_conv(x, g, bias, 2, flags, cuda_dev)
+        assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", f"small {case}")
+    else:
+        y = gpu_conv(x, g, bias, 2, flags, cuda_dev)
+        assert_close(y, oracle_conv(x, g, bias, 2, True), "f23", f"small {case}")
+
+
 @pytest.mark.parametrize("case", [
     (128, 200, 2, 0), (128, 200, 2, cwg.BF16), (128, 200, 2, cwg.TC_NOPAIR),
     (128, 200, 2, cwg.TC_FULL16), (96, 200, 4, cwg.BF16), (32, 40, 2, 0), (32, 40, 4, cwg.BF16),
