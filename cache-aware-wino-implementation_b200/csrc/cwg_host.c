@@ -265,15 +265,15 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
     out->threads = t.threads;
     out->smem_bytes = t.smem;
     out->tmem_cols = t.tmem_cols;
+    const int v = tc_variant(flags, mm, c_out);
+    const int bf = (flags & CWG_BF16) != 0, split = !(flags & CWG_NO_SPLIT);
     out->ctas = ((long long)n * th * tw + t.tiles - 1) / t.tiles * ((c_out + t.kb - 1) / t.kb) *
                 t.ctas_per_tile_block *
-                cwgk_tc_splits(n, c_in, c_out, h, w, mm, tc_variant(flags, mm, c_out),
-                               (flags & CWG_BF16) != 0, !(flags & CWG_NO_SPLIT), num_sms());
+                cwgk_tc_splits(n, c_in, c_out, h, w, mm, v, bf, split, num_sms());
     out->ctas_launched = out->ctas;
     out->order = CWG_ORDER_GRID;
-    if (n > 0 && cwgk_tc_plan(n, c_in, c_out, h, w, mm, tc_x3(mm, flags), tc_variant(flags, mm, c_out),
-                              (flags & CWG_BF16) != 0, !(flags & CWG_NO_SPLIT), num_sms(),
-                              &out->ctas_launched, &out->order) != 0) {
+    if (n > 0 && cwgk_tc_plan(n, c_in, c_out, h, w, mm, tc_x3(mm, flags), v, bf, split,
+                              num_sms(), &out->ctas_launched, &out->order) != 0) {
       out->ctas_launched = out->ctas;
       out->order = CWG_ORDER_GRID;
     }

@@ -1325,7 +1325,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
     const int S = n_items * nst;  // every stage of every item, in order
     // Two-pixel loads need an even row length (every pair then lies inside or
     // outside the image as a whole) and x aligned to two elements.
-    const bool pairs = ((W & 1) == 0) && ((reinterpret_cast<uintptr_t>(x) & (2 * sizeof(Tio) - 1)) == 0);
+    const bool pairs =
+        ((W & 1) == 0) && ((reinterpret_cast<uintptr_t>(x) & (2 * sizeof(Tio) - 1)) == 0);
 
     // The lane's tile in the current item: rank r holds B rows [0, N/2) = the
     // item's tiles [r N/2, (r + 1) N/2).  A group meets each item first at its
@@ -1495,8 +1496,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
         if (sn < S) load_stage(sn);
       }
     }
-    while (ep < n_items) ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
-                                           total_tiles, chunk, kb_count, relu, split) && ok;
+    while (ep < n_items)
+      ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
+                                         total_tiles, chunk, kb_count, relu, split) &&
+           ok;
     if (n_items == 0) named_bar_sync(kBarTmem, 32 + kEpiThreads);
   }
 
@@ -1654,7 +1657,8 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
   auto fn = wino_fused_tc_pair<M, X3, Tio, HM>;
   e = smem_attr_once<wino_fused_tc_pair<M, X3, Tio, HM>>(L::kSmem);
   if (e != cudaSuccess) return e;
-  const int resident = resident_pairs<wino_fused_tc_pair<M, X3, Tio, HM>>(G::kThreads, L::kSmem, sms);
+  const int resident =
+      resident_pairs<wino_fused_tc_pair<M, X3, Tio, HM>>(G::kThreads, L::kSmem, sms);
   const PairPlan plan = plan_pairs<M, HM>(total, gy, splits, resident);
   // tile indices, item counts and units are 32-bit in the kernel
   if (total * gy > 0x7fffffffLL || 2 * plan.pairs > 0x7fffffffLL || plan.gy > 65535)
