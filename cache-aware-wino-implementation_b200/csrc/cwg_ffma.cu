@@ -47,7 +47,10 @@ __global__ void wt_transform_ffma(const float *__restrict__ src, float *__restri
 //   * each warp runs the GEMM of FPW frequencies, every lane holding a TR x KR
 //     register block (tiles x output channels).
 // The epilogue regroups the frequency accumulators through shared memory and
-// applies At M A, bias and ReLU, storing NCHW.
+// applies At M A, bias and ReLU, storing NCHW.  With `slices` > 1 (fp32 only) the
+// steps are split into that many C_in ranges, one per CTA (blockIdx.z = image *
+// slices + slice): each CTA adds its partial At M A into the zeroed y with fp32
+// atomics, slice 0 adding the bias; ReLU, if any, then needs a second pass.
 template <int M, int TY, int TX, int KB, int CC, int FPW>
 struct FG {
   static constexpr int TD = M + 2, NF = TD * TD, T = TY * TX;
@@ -161,7 +164,7 @@ template <int M, int TY, int TX, int KB, int CC, int FPW, typename Tio>
 __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
     wino_fused_ffma(const Tio *__restrict__ x, const float *__restrict__ U,
                     const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
-                    int W, int tiles_y, int tiles_x, int relu) {
+                    int W, int tiles_y, int tiles_x, int relu, int slices) {
   using G = FG<M, TY, TX, KB, CC, FPW>;
   constexpr int TD = G::TD, T = G::T, NT = G::NT, KR = G::KR, TR = G::TR, KG = G::KG;
   extern __shared__ __align__(16) float smem[];
@@ -173,12 +176,14 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
   const int tg = lane / KG, kg = lane % KG;
   const int nbx = (tiles_x + TX - 1) / TX;
   const int by = blockIdx.x / nbx, bx = blockIdx.x - by * nbx;
-  const int k0 = blockIdx.y * KB, n = blockIdx.z;
+  // blockIdx.z = image * slices + C_in slice; a slice owns steps [st0, st1)
+  const int k0 = blockIdx.y * KB, n = blockIdx.z / slices, slice = blockIdx.z - n * slices;
   const int ty0 = by * TY, tx0 = bx * TX;
   const int iy0 = ty0 * M - 1, ix0 = tx0 * M - 1;
   const size_t plane = (size_t)H * W;
   const Tio *xn = x + (size_t)n * C * plane;
-  const int steps = (C + CC - 1) / CC;
+  const int steps = (C + CC - 1) / CC, per = (steps + slices - 1) / slices;
+  const int st0 = slice * per, st1 = min(steps, st0 + per);
   const bool u_vec = (K & 3) == 0;  // every U row starts on a 16-byte boundary
 
   // ---- U step s -> us buffer (s & 1), 16-byte chunks (scalar if K % 4 != 0)
@@ -238,16 +243,16 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
   const int part = warp % G::PARTS, tp = (warp / G::PARTS) * 32 + lane;
   const int tc = tp / T, tt = tp - tc * T, tyl = tt / TX, txl = tt - tyl * TX;
 
-  issue_u(0);
-  load_x(0);
-  for (int st = 0; st < steps; ++st) {
+  issue_u(st0);
+  load_x(st0);
+  for (int st = st0; st < st1; ++st) {
     // stage this step's halo, prefetch the next step
 #pragma unroll
     for (int j = 0; j < G::XPT; ++j) {
       const int i = tid + j * NT;
       if (i < G::XS) xs[i] = xr[j];
     }
-    if (st + 1 < steps) {
+    if (st + 1 < st1) {
       issue_u(st + 1);
       load_x(st + 1);
       cp_async_wait<1>();
@@ -316,7 +321,7 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
           for (int b2 = 0; b2 < TD; ++b2)
             mm[a][b2] = ms[((a * TD + b2) * KG + kgp) * (T + 1) + t];
         output_transform<M>(mm, yy);
-        const float bb = bias ? bias[k] : 0.f;
+        const float bb = (bias && slice == 0) ? bias[k] : 0.f;
         Tio *yk = y + ((size_t)n * K + k) * plane;
 #pragma unroll
         for (int i = 0; i < M; ++i)
@@ -325,8 +330,13 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
             const int oy = ty * M + i, ox = tx * M + j;
             if (oy < H && ox < W) {
               float v = yy[i][j] + bb;
-              if (relu) v = v < 0.f ? 0.f : v;
-              yk[(size_t)oy * W + ox] = from_f32<Tio>(v);
+              if (slices > 1) {
+                // partial sum of this slice into the zeroed y (fp32 only)
+                if constexpr (sizeof(Tio) == 4) atomicAdd(&yk[(size_t)oy * W + ox], v);
+              } else {
+                if (relu) v = v < 0.f ? 0.f : v;
+                yk[(size_t)oy * W + ox] = from_f32<Tio>(v);
+              }
             }
           }
       }
@@ -403,7 +413,7 @@ __global__ void __launch_bounds__(kTileThreads)
 // Configuration table + launch shims
 // ============================================================================
 typedef void (*ffma_fn)(const void *, const void *, const float *, void *, int, int, int, int,
-                        int, int, int);
+                        int, int, int, int);
 
 struct FfmaEntry {
   cwgk_ffma_cfg cfg;
@@ -431,6 +441,31 @@ constexpr int kNumFfma = sizeof(kFfma) / sizeof(kFfma[0]);
 static int fail(cudaError_t e) {
   t_cuda_error = (int)e;
   return -3; /* CWG_ECUDA */
+}
+
+// C_in slices for an fp32 layer whose grid fills at most a quarter of the SMs and
+// that has at least 8 steps: such a layer's few CTAs (one per SM: the kernels take
+// 72-168 registers a thread) walk all C_in steps one after another, ~2 us per
+// F(4,3) step.  One slice per idle SM, doubled (down to 4 steps a slice) while a
+// slice would keep more than 8 steps; at least 2 steps per slice, none empty.
+// Measured on B200 (N=1, fp32): 256->256 at 14x14 F(4,3) 70.9 -> 19.8 us,
+// 512->512 at 7x7 131.6 -> 48.3 us, 64->32 at 56x56 23.8 -> 14.6 us; grids above a
+// quarter of the SMs or shorter C_in lose more to the zeroing, the atomics and the
+// launches than the split saves (e.g. 128->128 at 56x56 F(4,3): 41.2 -> 50.7 us).
+// 1 = no split.
+static int ffma_slices(const cwgk_ffma_cfg &c, int n, int c_in, int c_out, int h, int w,
+                       int bf16, int allow_split, int sms) {
+  if (bf16 || !allow_split || n <= 0) return 1;
+  const long long tiles_y = (h + c.m - 1) / c.m, tiles_x = (w + c.m - 1) / c.m;
+  const long long grid = ((tiles_y + c.ty - 1) / c.ty) * ((tiles_x + c.tx - 1) / c.tx) *
+                         ((c_out + c.kb - 1) / c.kb) * n;
+  const int steps = (c_in + c.cc - 1) / c.cc;
+  if (4 * grid > sms || steps < 8) return 1;
+  long long s = (sms + grid - 1) / grid;
+  if (s > steps / 2) s = steps / 2;
+  if ((steps + s - 1) / s > 8) s = 2 * s < steps / 4 ? 2 * s : steps / 4;
+  const int per = (int)((steps + s - 1) / s);
+  return (steps + per - 1) / per;
 }
 
 }  // namespace cwg
@@ -473,8 +508,15 @@ int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m,
   return e == cudaSuccess ? 0 : fail(e);
 }
 
+int cwgk_ffma_splits(int cfg_idx, int n, int c_in, int c_out, int h, int w, int bf16,
+                     int allow_split, int sms) {
+  if (cfg_idx < 0 || cfg_idx >= kNumFfma) return 1;
+  return ffma_slices(kFfma[cfg_idx].cfg, n, c_in, c_out, h, w, bf16, allow_split, sms);
+}
+
 int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
-                   int c_in, int c_out, int h, int w, int bf16, int relu, void *stream) {
+                   int c_in, int c_out, int h, int w, int bf16, int relu, int allow_split,
+                   void *stream) {
   if (cfg_idx < 0 || cfg_idx >= kNumFfma) return -1;
   const FfmaEntry &e = kFfma[cfg_idx];
   const int m = e.cfg.m;
@@ -483,17 +525,36 @@ int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias,
                                  ((tiles_x + e.cfg.tx - 1) / e.cfg.tx));
   const unsigned gy = (unsigned)((c_out + e.cfg.kb - 1) / e.cfg.kb);
   if (n > 65535 || gy > 65535) return -2;
+  int slices = 1;
+  if (allow_split && !bf16) {
+    int dev = 0, sms = 0;
+    cudaError_t qe = cudaGetDevice(&dev);
+    if (qe == cudaSuccess)
+      qe = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (qe != cudaSuccess) return fail(qe);
+    slices = ffma_slices(e.cfg, n, c_in, c_out, h, w, bf16, allow_split, sms);
+  }
+  if ((long long)n * slices > 65535) slices = 1;
   const void *fn = bf16 ? e.fn_bf16 : e.fn_f32;
   static std::atomic<unsigned long long> attr_done[kNumFfma][2];
   cudaError_t err = smem_attr_once(attr_done[cfg_idx][bf16 ? 1 : 0], fn, e.cfg.smem);
   if (err != cudaSuccess) return fail(err);
-  void *args[] = {(void *)&x,  (void *)&U, (void *)&bias,    (void *)&y,       (void *)&c_in,
-                  (void *)&c_out, (void *)&h, (void *)&w, (void *)&tiles_y, (void *)&tiles_x,
-                  (void *)&relu};
-  err = cudaLaunchKernel(fn, dim3(gx, gy, (unsigned)n), dim3((unsigned)e.cfg.threads), args,
-                         (size_t)e.cfg.smem, (cudaStream_t)stream);
+  cudaStream_t s = (cudaStream_t)stream;
+  // split: y zeroed and accumulated; with ReLU the bias joins in the second pass
+  const float *kbias = (slices > 1 && relu) ? nullptr : bias;
+  int krelu = slices > 1 ? 0 : relu;
+  if (slices > 1 &&
+      (err = cudaMemsetAsync(y, 0, (size_t)n * c_out * h * w * sizeof(float), s)) != cudaSuccess)
+    return fail(err);
+  void *args[] = {(void *)&x,     (void *)&U, (void *)&kbias,   (void *)&y,
+                  (void *)&c_in,  (void *)&c_out, (void *)&h,   (void *)&w,
+                  (void *)&tiles_y, (void *)&tiles_x, (void *)&krelu, (void *)&slices};
+  err = cudaLaunchKernel(fn, dim3(gx, gy, (unsigned)(n * slices)),
+                         dim3((unsigned)e.cfg.threads), args, (size_t)e.cfg.smem, s);
   cwgk_count_launch();
-  return err == cudaSuccess ? 0 : fail(err);
+  if (err != cudaSuccess) return fail(err);
+  if (slices > 1 && relu) return cwgk_bias_relu((float *)y, bias, n, c_out, h, w, 1, stream);
+  return 0;
 }
 
 int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,

@@ -292,7 +292,8 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
     out->order = CWG_ORDER_GRID;
   } else {
     cwgk_ffma_cfg c;
-    if (pick_ffma(n, c_out, h, w, mm, &c) < 0) return CWG_EUNSUPPORTED;
+    const int idx = pick_ffma(n, c_out, h, w, mm, &c);
+    if (idx < 0) return CWG_EUNSUPPORTED;
     out->tiles_per_cta = c.ty * c.tx;
     out->cout_per_cta = c.kb;
     out->cin_chunk = c.cc;
@@ -300,7 +301,9 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
     out->smem_bytes = c.smem;
     out->tmem_cols = 0;
     out->ctas = (long long)n * ((th + c.ty - 1) / c.ty) * ((tw + c.tx - 1) / c.tx) *
-                ((c_out + c.kb - 1) / c.kb);
+                ((c_out + c.kb - 1) / c.kb) *
+                cwgk_ffma_splits(idx, n, c_in, c_out, h, w, (flags & CWG_BF16) != 0,
+                                 !(flags & CWG_NO_SPLIT), num_sms());
     out->ctas_launched = out->ctas;
     out->order = CWG_ORDER_GRID;
   }
@@ -360,7 +363,8 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   cwgk_ffma_cfg cfg;
   const int idx = pick_ffma(n, c_out, h, w, mm, &cfg);
   if (idx < 0) return CWG_EUNSUPPORTED;
-  return cwgk_conv_ffma(idx, x, U, bias, y, n, c_in, c_out, h, w, bf16, relu, stream);
+  return cwgk_conv_ffma(idx, x, U, bias, y, n, c_in, c_out, h, w, bf16, relu,
+                        !(flags & CWG_NO_SPLIT), stream);
 }
 
 /* ---- per-thread context: staging for the per-tile calls, copy streams ---- */

@@ -65,14 +65,24 @@ int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m,
 int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int m, int layout,
                              int from_ref, void *stream);
 
-/* FFMA fused convolution with configuration `cfg_idx`. */
 /* F(2,3) for layers of 1-4 input channels (csrc/cwg_small.cu): one thread per tile,
  * 64 output channels per CTA, weights in the CUDA-core layout. */
 int cwgk_conv_small(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
                     int c_out, int h, int w, int bf16, int relu, void *stream);
 
+/* FFMA fused convolution with configuration `cfg_idx`.  allow_split: an fp32 layer
+ * whose grid leaves SMs idle splits its C_in steps across CTAs (y zeroed, partial
+ * sums added atomically, bias with slice 0 or, with ReLU, in a second pass). */
 int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
-                   int c_in, int c_out, int h, int w, int bf16, int relu, void *stream);
+                   int c_in, int c_out, int h, int w, int bf16, int relu, int allow_split,
+                   void *stream);
+/* C_in slices the FFMA path uses for this layer (1 = no split); `sms` SMs. */
+int cwgk_ffma_splits(int cfg_idx, int n, int c_in, int c_out, int h, int w, int bf16,
+                     int allow_split, int sms);
+/* bias + ReLU in place over the n*c_out fp32 planes of h*w in y (after a split
+ * reduction). */
+int cwgk_bias_relu(float *y, const float *bias, int n, int c_out, int h, int w, int relu,
+                   void *stream);
 
 /* tcgen05 fused convolution F(m x m, 3x3) (C_in padded to 16 and C_out to the
  * channel block by the weight layout), kernel `variant` (CWGK_TC_*; the

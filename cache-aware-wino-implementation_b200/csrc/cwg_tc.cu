@@ -1551,6 +1551,20 @@ __global__ void bias_relu_pass(float *__restrict__ y, const float *__restrict__ 
   }
 }
 
+// bias_relu_pass over n*k planes of h*w floats: one grid row per plane (up to
+// 65535), the columns capped so that the grid stays near 8 CTAs per SM.
+static cudaError_t launch_bias_relu(float *y, const float *bias, int n, int k, int h, int w,
+                                    int relu, int sms, cudaStream_t s) {
+  cwgk_count_launch();
+  const long long plane = (long long)h * w, planes = (long long)n * k;
+  const unsigned gy = (unsigned)(planes < 65535 ? planes : 65535);
+  long long bx = (plane / 4 + 255) / 256;
+  if (bx < 1) bx = 1;
+  if (bx * gy > 8LL * sms) bx = (8LL * sms + gy - 1) / gy;
+  bias_relu_pass<<<dim3((unsigned)bx, gy), 256, 0, s>>>(y, bias, k, plane, planes, relu);
+  return cudaGetLastError();
+}
+
 // C_in slices for a layer whose CTA pairs would leave three quarters of the TPCs
 // idle: each slice keeps at least 2 stages.  1 = no split.  (Above that occupancy
 // the extra zeroing, atomics and bias pass cost more than the shorter C_in loop
@@ -1670,17 +1684,7 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
                       tiles_x, (int)total, relu, per, splits > 1, (int)plan.chunk,
                       plan.kb_count);
   if ((e = cudaGetLastError()) != cudaSuccess || splits == 1) return e;
-  if (relu) {
-    cwgk_count_launch();
-    const long long plane = (long long)h * w, planes = (long long)n * k;
-    const unsigned gy = (unsigned)(planes < 65535 ? planes : 65535);
-    long long bx = (plane / 4 + 255) / 256;
-    if (bx < 1) bx = 1;
-    if (bx * gy > 8LL * sms) bx = (8LL * sms + gy - 1) / gy;
-    bias_relu_pass<<<dim3((unsigned)bx, gy), 256, 0, s>>>((float *)y, bias, k, plane, planes,
-                                                          relu);
-    e = cudaGetLastError();
-  }
+  if (relu) e = launch_bias_relu((float *)y, bias, n, k, h, w, relu, sms, s);
   return e;
 }
 
@@ -1823,6 +1827,20 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
 #undef CWG_WT
   cwgk_count_launch();
   const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cwgk_set_cuda_error((int)e);
+    return -3;
+  }
+  return 0;
+}
+
+int cwgk_bias_relu(float *y, const float *bias, int n, int c_out, int h, int w, int relu,
+                   void *stream) {
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess)
+    e = tc::launch_bias_relu(y, bias, n, c_out, h, w, relu, sms, (cudaStream_t)stream);
   if (e != cudaSuccess) {
     cwgk_set_cuda_error((int)e);
     return -3;

@@ -70,10 +70,26 @@ def test_selector_auto_m_and_bf16():
 
 def test_selector_grid_covers_layer():
     for (n, c, k, h, w, m) in [(1, 32, 32, 56, 56, 2), (3, 16, 17, 7, 5, 4), (2, 64, 64, 1, 1, 2)]:
-        ch = cwg.select(n, c, k, h, w, m, cwg.FORCE_FFMA)
+        ch = cwg.select(n, c, k, h, w, m, cwg.FORCE_FFMA | cwg.NO_SPLIT)
         th, tw = -(-h // ch.m), -(-w // ch.m)
         side = int(round(ch.tiles_per_cta ** 0.5))
         assert ch.ctas == n * (-(-th // side)) * (-(-tw // side)) * (-(-k // ch.cout_per_cta))
+
+
+def test_selector_ffma_split():
+    """fp32 layers whose CUDA-core grid fills at most a quarter of the SMs and that
+    have at least 8 C_in steps split them: one slice per idle SM, doubled while a
+    slice would keep more than 8 steps, at least 2 steps per slice.  bf16 layers,
+    NO_SPLIT, shorter C_in and larger grids do not."""
+    for (c, k, h, m, slices) in [(256, 256, 14, 4, 8), (512, 512, 7, 4, 10), (64, 32, 56, 4, 4),
+                                 (512, 32, 7, 2, 32)]:
+        one = cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA | cwg.NO_SPLIT)
+        ch = cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA)
+        assert ch.ctas == slices * one.ctas, (c, k, h, m)
+        assert cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA | cwg.BF16).ctas == one.ctas
+    for (c, k, h, m) in [(128, 128, 56, 4), (64, 64, 56, 4), (32, 32, 56, 4), (64, 32, 56, 2)]:
+        assert (cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA).ctas ==
+                cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA | cwg.NO_SPLIT).ctas), (c, k, h, m)
 
 
 @pytest.mark.parametrize("args,status", [

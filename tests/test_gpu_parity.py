@@ -466,6 +466,29 @@ def test_split_reduction_small_layers(cuda_dev, case):
     assert_close(y, y1, "f23", f"split vs unsplit {case}")
 
 
+@pytest.mark.parametrize("case", [(1, 256, 256, 14, 14, 4, True, False), (1, 512, 512, 7, 7, 4, True, True),
+                                  (1, 64, 32, 56, 56, 4, False, True), (1, 200, 48, 23, 19, 4, True, False),
+                                  (1, 128, 40, 30, 30, 6, True, True), (1, 96, 24, 17, 9, 2, True, True)],
+                         ids=lambda c: "x".join(map(str, c)))
+def test_ffma_split_reduction(cuda_dev, case):
+    """Single-image fp32 layers on the CUDA-core kernel whose grid leaves most SMs
+    idle split their C_in steps across CTAs: same result as the unsplit kernel and
+    the reference, with and without bias and ReLU."""
+    n, c, k, h, w, m, use_bias, relu = case
+    rng = np.random.default_rng(sum(case) + 900)
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32) if use_bias else None
+    fl = cwg.FORCE_FFMA | (cwg.RELU if relu else 0)
+    sel = cwg.select(n, c, k, h, w, m, fl)
+    assert sel.path == cwg.PATH_FFMA and sel.ctas > cwg.select(n, c, k, h, w, m, fl | cwg.NO_SPLIT).ctas
+    y = gpu_conv(x, g, bias, m, fl, cuda_dev)
+    y1 = gpu_conv(x, g, bias, m, fl | cwg.NO_SPLIT, cuda_dev)
+    tol = {2: "f23", 4: "f43", 6: "f63"}[m]
+    assert_close(y, oracle_conv(x, g, bias, m, relu), tol, f"ffma split {case}")
+    assert_close(y, y1, tol, f"ffma split vs unsplit {case}")
+
+
 def test_bounded_wait_times_out_and_context_survives(cuda_dev):
     """A device wait on a barrier nothing arrives on gives up after its limit, the host
     reads CWG_ETIMEOUT, the status clears, and the next layer runs normally."""
