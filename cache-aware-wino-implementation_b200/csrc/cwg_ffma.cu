@@ -443,31 +443,6 @@ static int fail(cudaError_t e) {
   return -3; /* CWG_ECUDA */
 }
 
-// C_in slices for an fp32 layer whose grid fills at most a quarter of the SMs and
-// that has at least 8 steps: such a layer's few CTAs (one per SM: the kernels take
-// 72-168 registers a thread) walk all C_in steps one after another, ~2 us per
-// F(4,3) step.  One slice per idle SM, doubled (down to 4 steps a slice) while a
-// slice would keep more than 8 steps; at least 2 steps per slice, none empty.
-// Measured on B200 (N=1, fp32): 256->256 at 14x14 F(4,3) 70.9 -> 19.8 us,
-// 512->512 at 7x7 131.6 -> 48.3 us, 64->32 at 56x56 23.8 -> 14.6 us; grids above a
-// quarter of the SMs or shorter C_in lose more to the zeroing, the atomics and the
-// launches than the split saves (e.g. 128->128 at 56x56 F(4,3): 41.2 -> 50.7 us).
-// 1 = no split.
-static int ffma_slices(const cwgk_ffma_cfg &c, int n, int c_in, int c_out, int h, int w,
-                       int bf16, int allow_split, int sms) {
-  if (bf16 || !allow_split || n <= 0) return 1;
-  const long long tiles_y = (h + c.m - 1) / c.m, tiles_x = (w + c.m - 1) / c.m;
-  const long long grid = ((tiles_y + c.ty - 1) / c.ty) * ((tiles_x + c.tx - 1) / c.tx) *
-                         ((c_out + c.kb - 1) / c.kb) * n;
-  const int steps = (c_in + c.cc - 1) / c.cc;
-  if (4 * grid > sms || steps < 8) return 1;
-  long long s = (sms + grid - 1) / grid;
-  if (s > steps / 2) s = steps / 2;
-  if ((steps + s - 1) / s > 8) s = 2 * s < steps / 4 ? 2 * s : steps / 4;
-  const int per = (int)((steps + s - 1) / s);
-  return (steps + per - 1) / per;
-}
-
 }  // namespace cwg
 
 using namespace cwg;
@@ -508,14 +483,8 @@ int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m,
   return e == cudaSuccess ? 0 : fail(e);
 }
 
-int cwgk_ffma_splits(int cfg_idx, int n, int c_in, int c_out, int h, int w, int bf16,
-                     int allow_split, int sms) {
-  if (cfg_idx < 0 || cfg_idx >= kNumFfma) return 1;
-  return ffma_slices(kFfma[cfg_idx].cfg, n, c_in, c_out, h, w, bf16, allow_split, sms);
-}
-
 int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
-                   int c_in, int c_out, int h, int w, int bf16, int relu, int allow_split,
+                   int c_in, int c_out, int h, int w, int bf16, int relu, int slices,
                    void *stream) {
   if (cfg_idx < 0 || cfg_idx >= kNumFfma) return -1;
   const FfmaEntry &e = kFfma[cfg_idx];
@@ -525,16 +494,13 @@ int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias,
                                  ((tiles_x + e.cfg.tx - 1) / e.cfg.tx));
   const unsigned gy = (unsigned)((c_out + e.cfg.kb - 1) / e.cfg.kb);
   if (n > 65535 || gy > 65535) return -2;
-  int slices = 1;
-  if (allow_split && !bf16) {
-    int dev = 0, sms = 0;
-    cudaError_t qe = cudaGetDevice(&dev);
-    if (qe == cudaSuccess)
-      qe = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (qe != cudaSuccess) return fail(qe);
-    slices = ffma_slices(e.cfg, n, c_in, c_out, h, w, bf16, allow_split, sms);
-  }
-  if ((long long)n * slices > 65535) slices = 1;
+  // slices: fp32 only, at most one per step, none empty
+  const int steps = (c_in + e.cfg.cc - 1) / e.cfg.cc;
+  if (slices < 1 || bf16) slices = 1;
+  if (slices > steps) slices = steps;
+  const int per = (steps + slices - 1) / slices;
+  slices = (steps + per - 1) / per;
+  if ((long long)n * slices > 65535) return -2;
   const void *fn = bf16 ? e.fn_bf16 : e.fn_f32;
   static std::atomic<unsigned long long> attr_done[kNumFfma][2];
   cudaError_t err = smem_attr_once(attr_done[cfg_idx][bf16 ? 1 : 0], fn, e.cfg.smem);

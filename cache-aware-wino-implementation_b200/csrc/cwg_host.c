@@ -185,29 +185,51 @@ static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
   }
 }
 
-/* Picks the FFMA configuration for a layer (index into the shim's table):
- * the widest output-channel block that still gives at least one CTA per SM. */
 static int find_ffma_ty(int m, int kb, int ty, cwgk_ffma_cfg *c) {
   const int ncfg = cwgk_ffma_num_cfgs();
   for (int i = 0; i < ncfg; ++i)
     if (cwgk_ffma_get_cfg(i, c) == 0 && c->m == m && c->kb == kb && c->ty == ty) return i;
   return -1;
 }
-static int find_ffma(int m, int kb, cwgk_ffma_cfg *c) { return find_ffma_ty(m, kb, 4, c); }
 
 /* F(2,3) layers of 1-4 input channels (an RGB input layer) run the one-tile-per-
  * thread kernel: they are bound by writing the output planes, and the general
  * kernel's per-CTA staging of 8-channel weight chunks costs more than the math. */
 static int small_cin(int c_in, int m) { return m == 2 && c_in <= 4; }
 
-static int pick_ffma(int n, int c_out, int h, int w, int m, cwgk_ffma_cfg *cfg_out) {
+/* Cost of one CTA of the 4x4-tile CUDA-core kernel, c0 + steps * b microseconds
+ * for `steps` 8-channel input steps, fitted to B200 sweeps of single-image 56x56
+ * layers over channel block x C_in slices (6 % rms).  The kernels run one CTA per
+ * SM (72-168 registers a thread), so a grid of G CTAs takes ceil(G / SMs) such
+ * rounds.  A C_in split adds the zeroing of y and its atomics, and with ReLU the
+ * bias/ReLU pass. */
+typedef struct {
+  int m, kb;
+  double c0, b;
+} ffma_cost;
+static const ffma_cost kFfmaCost[] = {
+    {2, 16, 1.8, 0.92}, {2, 32, 2.1, 1.10}, {2, 64, 2.5, 1.66}, {4, 16, 4.3, 1.95},
+    {4, 32, 4.5, 2.56}, {4, 64, 6.3, 4.27}, {6, 16, 6.0, 4.6},
+};
+#define FFMA_SPLIT_US 2.4
+#define FFMA_RELU_PASS_US 3.5
+
+/* Picks the FFMA configuration for a layer (index into the shim's table) and its
+ * C_in slices (1 unless fp32 and allowed):
+ *   - large layers whose grid of 8x8-tile blocks of 32 channels still fills every
+ *     SM take that kernel: a CTA's weight chunk then serves 64 tiles instead of
+ *     16, and each CTA pays its load / transform / store latency once (a 3->64
+ *     layer at 224x224, 32 images: 521 vs 791 us);
+ *   - otherwise the (channel block, slices) of least modelled time (kFfmaCost):
+ *     wide blocks use fewer instructions per output channel, narrow blocks and
+ *     slices fill more SMs.  Single-image F(4,3) at 56x56 (us, model pick vs the
+ *     previous widest-block-filling-the-SMs rule): 64->64 14.7 vs 23.7, 128->128
+ *     31.3 vs 39.6. */
+static int pick_ffma(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
+                     cwgk_ffma_cfg *cfg_out, int *slices_out) {
   const int sms = num_sms();
   const long long th = (h + m - 1) / m, tw = (w + m - 1) / m;
-  /* Large images first try 8x8-tile blocks of 32 channels: a CTA's weight
-   * chunk then serves 64 tiles instead of 16, and the grid has a quarter of
-   * the CTAs, each of which pays its load / transform / store latency once
-   * (a 3->64 layer at 224x224, 32 images: 521 vs 791 us).  Only when that grid
-   * still fills every SM. */
+  if (slices_out) *slices_out = 1;
   if (c_out >= 32) {
     cwgk_ffma_cfg c;
     const int idx = find_ffma_ty(m, 32, 8, &c);
@@ -220,23 +242,45 @@ static int pick_ffma(int n, int c_out, int h, int w, int m, cwgk_ffma_cfg *cfg_o
       }
     }
   }
-  int kb = c_out >= 64 ? 64 : (c_out > 16 ? 32 : 16);
-  for (;;) {
+  const int can_split = !(flags & (CWG_BF16 | CWG_NO_SPLIT));
+  const int relu = (flags & CWG_RELU) != 0;
+  int best = -1, best_s = 1;
+  double best_t = 0.0;
+  cwgk_ffma_cfg best_c;
+  memset(&best_c, 0, sizeof(best_c));
+  static const int kbs[3] = {64, 32, 16}; /* ties keep the wider block */
+  for (int i = 0; i < 3; ++i) {
     cwgk_ffma_cfg c;
-    const int idx = find_ffma(m, kb, &c);
-    if (idx < 0) {  /* no kernel with this channel block for this m: try a smaller one */
-      if (kb == 16) return -1;
-      kb /= 2;
-      continue;
-    }
-    const long long ctas = (long long)n * ((th + c.ty - 1) / c.ty) * ((tw + c.tx - 1) / c.tx) *
+    const int idx = find_ffma_ty(m, kbs[i], 4, &c);
+    if (idx < 0) continue;
+    const ffma_cost *cost = NULL;
+    for (size_t j = 0; j < sizeof(kFfmaCost) / sizeof(kFfmaCost[0]); ++j)
+      if (kFfmaCost[j].m == m && kFfmaCost[j].kb == c.kb) cost = &kFfmaCost[j];
+    if (!cost) continue;
+    const long long grid = (long long)n * ((th + c.ty - 1) / c.ty) * ((tw + c.tx - 1) / c.tx) *
                            ((c_out + c.kb - 1) / c.kb);
-    if (ctas >= sms || kb == 16) {
-      if (cfg_out) *cfg_out = c;
-      return idx;
+    const int steps = (c_in + c.cc - 1) / c.cc;
+    /* splitting a grid that already fills the SMs only adds rounds */
+    const int max_s = (can_split && grid < sms) ? steps : 1;
+    for (int s = 1; s <= max_s; ++s) {
+      const int per = (steps + s - 1) / s;
+      if ((steps + per - 1) / per != s) continue; /* same steps per slice as a smaller s */
+      if ((long long)n * s > 65535) break;
+      const double rounds = (double)((grid * s + sms - 1) / sms);
+      const double t = rounds * (cost->c0 + per * cost->b) +
+                       (s > 1 ? FFMA_SPLIT_US + (relu ? FFMA_RELU_PASS_US : 0.0) : 0.0);
+      if (best < 0 || t < best_t) {
+        best = idx;
+        best_s = s;
+        best_t = t;
+        best_c = c;
+      }
     }
-    kb /= 2;
   }
+  if (best < 0) return -1;
+  if (cfg_out) *cfg_out = best_c;
+  if (slices_out) *slices_out = best_s;
+  return best;
 }
 
 int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
@@ -292,8 +336,8 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
     out->order = CWG_ORDER_GRID;
   } else {
     cwgk_ffma_cfg c;
-    const int idx = pick_ffma(n, c_out, h, w, mm, &c);
-    if (idx < 0) return CWG_EUNSUPPORTED;
+    int slices = 1;
+    if (pick_ffma(n, c_in, c_out, h, w, mm, flags, &c, &slices) < 0) return CWG_EUNSUPPORTED;
     out->tiles_per_cta = c.ty * c.tx;
     out->cout_per_cta = c.kb;
     out->cin_chunk = c.cc;
@@ -301,9 +345,7 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
     out->smem_bytes = c.smem;
     out->tmem_cols = 0;
     out->ctas = (long long)n * ((th + c.ty - 1) / c.ty) * ((tw + c.tx - 1) / c.tx) *
-                ((c_out + c.kb - 1) / c.kb) *
-                cwgk_ffma_splits(idx, n, c_in, c_out, h, w, (flags & CWG_BF16) != 0,
-                                 !(flags & CWG_NO_SPLIT), num_sms());
+                ((c_out + c.kb - 1) / c.kb) * slices;
     out->ctas_launched = out->ctas;
     out->order = CWG_ORDER_GRID;
   }
@@ -361,10 +403,10 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   if (small_cin(c_in, mm))
     return cwgk_conv_small(x, U, bias, y, n, c_in, c_out, h, w, bf16, relu, stream);
   cwgk_ffma_cfg cfg;
-  const int idx = pick_ffma(n, c_out, h, w, mm, &cfg);
+  int slices = 1;
+  const int idx = pick_ffma(n, c_in, c_out, h, w, mm, flags, &cfg, &slices);
   if (idx < 0) return CWG_EUNSUPPORTED;
-  return cwgk_conv_ffma(idx, x, U, bias, y, n, c_in, c_out, h, w, bf16, relu,
-                        !(flags & CWG_NO_SPLIT), stream);
+  return cwgk_conv_ffma(idx, x, U, bias, y, n, c_in, c_out, h, w, bf16, relu, slices, stream);
 }
 
 /* ---- per-thread context: staging for the per-tile calls, copy streams ---- */

@@ -70,15 +70,12 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
 int cwgk_conv_small(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
                     int c_out, int h, int w, int bf16, int relu, void *stream);
 
-/* FFMA fused convolution with configuration `cfg_idx`.  allow_split: an fp32 layer
- * whose grid leaves SMs idle splits its C_in steps across CTAs (y zeroed, partial
+/* FFMA fused convolution with configuration `cfg_idx`.  slices > 1 (fp32 only)
+ * splits the C_in steps across that many CTAs per tile block (y zeroed, partial
  * sums added atomically, bias with slice 0 or, with ReLU, in a second pass). */
 int cwgk_conv_ffma(int cfg_idx, const void *x, const void *U, const float *bias, void *y, int n,
-                   int c_in, int c_out, int h, int w, int bf16, int relu, int allow_split,
+                   int c_in, int c_out, int h, int w, int bf16, int relu, int slices,
                    void *stream);
-/* C_in slices the FFMA path uses for this layer (1 = no split); `sms` SMs. */
-int cwgk_ffma_splits(int cfg_idx, int n, int c_in, int c_out, int h, int w, int bf16,
-                     int allow_split, int sms);
 /* bias + ReLU in place over the n*c_out fp32 planes of h*w in y (after a split
  * reduction). */
 int cwgk_bias_relu(float *y, const float *bias, int n, int c_out, int h, int w, int relu,

@@ -76,20 +76,34 @@ def test_selector_grid_covers_layer():
         assert ch.ctas == n * (-(-th // side)) * (-(-tw // side)) * (-(-k // ch.cout_per_cta))
 
 
+def ffma_slices(ch, n, k, h, w):
+    """C_in slices of a CUDA-core choice: CTAs over the grid of its tile and channel blocks."""
+    th, tw = -(-h // ch.m), -(-w // ch.m)
+    side = int(round(ch.tiles_per_cta ** 0.5))
+    grid = n * (-(-th // side)) * (-(-tw // side)) * (-(-k // ch.cout_per_cta))
+    assert ch.ctas % grid == 0
+    return ch.ctas // grid
+
+
 def test_selector_ffma_split():
-    """fp32 layers whose CUDA-core grid fills at most a quarter of the SMs and that
-    have at least 8 C_in steps split them: one slice per idle SM, doubled while a
-    slice would keep more than 8 steps, at least 2 steps per slice.  bf16 layers,
-    NO_SPLIT, shorter C_in and larger grids do not."""
-    for (c, k, h, m, slices) in [(256, 256, 14, 4, 8), (512, 512, 7, 4, 10), (64, 32, 56, 4, 4),
-                                 (512, 32, 7, 2, 32)]:
-        one = cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA | cwg.NO_SPLIT)
+    """The CUDA-core path picks its channel block and C_in slices together from a
+    per-CTA cost model: single-image deep layers split (fp32 only, at most one
+    slice per 8-channel step, CTAs within one round of the SMs); bf16 layers,
+    NO_SPLIT and grids that fill the SMs do not."""
+    sms = 148
+    for (c, k, h, m) in [(256, 256, 14, 4), (512, 512, 7, 4), (64, 32, 56, 4), (512, 32, 7, 2),
+                         (128, 40, 30, 6), (128, 128, 56, 4)]:
         ch = cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA)
-        assert ch.ctas == slices * one.ctas, (c, k, h, m)
-        assert cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA | cwg.BF16).ctas == one.ctas
-    for (c, k, h, m) in [(128, 128, 56, 4), (64, 64, 56, 4), (32, 32, 56, 4), (64, 32, 56, 2)]:
-        assert (cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA).ctas ==
-                cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA | cwg.NO_SPLIT).ctas), (c, k, h, m)
+        s = ffma_slices(ch, 1, k, h, h)
+        assert 2 <= s <= -(-c // 8) and ch.ctas <= sms, (c, k, h, m, s, ch.ctas)
+        for fl in (cwg.BF16, cwg.NO_SPLIT):
+            assert ffma_slices(cwg.select(1, c, k, h, h, m, cwg.FORCE_FFMA | fl), 1, k, h, h) == 1
+    for (n, c, k, h, m) in [(64, 32, 32, 56, 2), (64, 128, 128, 56, 4), (2, 128, 128, 60, 6),
+                            (1, 16, 32, 56, 2), (1, 32, 32, 56, 2)]:
+        ch = cwg.select(n, c, k, h, h, m, cwg.FORCE_FFMA)
+        assert ffma_slices(ch, n, k, h, h) == 1, (n, c, k, h, m)
+    # large layers keep the widest channel block
+    assert cwg.select(64, 128, 128, 56, 56, 4, cwg.FORCE_FFMA).cout_per_cta == 64
 
 
 @pytest.mark.parametrize("args,status", [

@@ -481,7 +481,9 @@ def test_ffma_split_reduction(cuda_dev, case):
     bias = rng.uniform(-0.1, 0.1, k).astype(np.float32) if use_bias else None
     fl = cwg.FORCE_FFMA | (cwg.RELU if relu else 0)
     sel = cwg.select(n, c, k, h, w, m, fl)
-    assert sel.path == cwg.PATH_FFMA and sel.ctas > cwg.select(n, c, k, h, w, m, fl | cwg.NO_SPLIT).ctas
+    blocks = n * (-(-h // (4 * m))) * (-(-w // (4 * m)))  # 4x4 output tiles per CTA
+    assert sel.path == cwg.PATH_FFMA and sel.tiles_per_cta == 16
+    assert sel.ctas > blocks * (-(-k // sel.cout_per_cta))  # C_in slices
     y = gpu_conv(x, g, bias, m, fl, cuda_dev)
     y1 = gpu_conv(x, g, bias, m, fl | cwg.NO_SPLIT, cuda_dev)
     tol = {2: "f23", 4: "f43", 6: "f63"}[m]
