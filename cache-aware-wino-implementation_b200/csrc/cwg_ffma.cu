@@ -212,20 +212,32 @@ __global__ void __launch_bounds__(FG<M, TY, TX, KB, CC, FPW>::NT, 1)
     cp_async_commit();
   };
   // ---- input halo of step s -> registers (stored to xs at the start of step s)
+  // per element, fixed across steps: (window row << 10) | (window column << 4) |
+  // chunk channel, or -1 outside the image / past the halo
   float xr[G::XPT];
+  int xpk[G::XPT];
+  static_assert(G::HR <= 64 && G::WR <= 64 && CC <= 16, "halo coordinates pack into 16 bits");
+#pragma unroll
+  for (int j = 0; j < G::XPT; ++j) {
+    const int i = tid + j * NT;
+    int pk = -1;
+    if (i < G::XS) {
+      const int c = i / (G::HR * G::WR), rem = i - c * (G::HR * G::WR);
+      const int r = rem / G::WR, s2 = rem - r * G::WR;
+      const int iy = iy0 + r, ix = ix0 + s2;
+      if (iy >= 0 && iy < H && ix >= 0 && ix < W) pk = (r << 10) | (s2 << 4) | c;
+    }
+    xpk[j] = pk;
+  }
   auto load_x = [&](int st) {
-    const int c0 = st * CC;
+    const int cl = C - st * CC;  // chunk channels c < cl exist
 #pragma unroll
     for (int j = 0; j < G::XPT; ++j) {
-      const int i = tid + j * NT;
+      const int pk = xpk[j];
       float v = 0.f;
-      if (i < G::XS) {
-        const int c = i / (G::HR * G::WR), rem = i - c * (G::HR * G::WR);
-        const int r = rem / G::WR, s2 = rem - r * G::WR;
-        const int iy = iy0 + r, ix = ix0 + s2;
-        if (c0 + c < C && iy >= 0 && iy < H && ix >= 0 && ix < W)
-          v = to_f32(xn[(size_t)(c0 + c) * plane + (size_t)iy * W + ix]);
-      }
+      if (pk >= 0 && (pk & 15) < cl)
+        v = to_f32(xn[(size_t)(st * CC + (pk & 15)) * plane +
+                      (size_t)(iy0 + (pk >> 10)) * W + (ix0 + ((pk >> 4) & 63))]);
       xr[j] = v;
     }
   };
@@ -433,7 +445,8 @@ static const FfmaEntry kFfma[] = {
     CWG_FFMA_ENTRY(4, 4, 4, 16, 8, 3), CWG_FFMA_ENTRY(4, 4, 4, 32, 8, 3),
     CWG_FFMA_ENTRY(4, 4, 4, 64, 8, 3),
     // F(6,3): a 32-channel block spills ~290 B per thread (64 accumulators beside
-    // the 8x8 window rows); the 16-channel block keeps it to ~80 B.
+    // the 8x8 window rows); the 16-channel block fits in 128 registers but for a
+    // few bytes.
     CWG_FFMA_ENTRY(6, 4, 4, 16, 8, 4),
 };
 constexpr int kNumFfma = sizeof(kFfma) / sizeof(kFfma[0]);
