@@ -491,6 +491,51 @@ def test_ffma_split_reduction(cuda_dev, case):
     assert_close(y, y1, tol, f"ffma split vs unsplit {case}")
 
 
+def _random_cases(count, seed=2024):
+    """Seeded layer shapes across every kernel the selector can pick: tensor-core
+    pairs (both channel counts >= 64), CUDA-core blocks with or without C_in slices,
+    the 1-4 input-channel kernel; fp32 and bf16, odd sizes, bias and ReLU on or off."""
+    rng = np.random.default_rng(seed)
+    cases = []
+    for i in range(count):
+        regime = i % 3
+        bf16 = bool(rng.random() < 0.3)
+        if regime == 0:  # tensor cores
+            c, k = int(rng.integers(64, 145)), int(rng.integers(64, 145))
+            m = 4 if bf16 and rng.random() < 0.5 else 2
+        elif regime == 1:  # CUDA cores
+            c, k = int(rng.integers(5, 97)), int(rng.integers(1, 64))
+            m = int(rng.choice([2, 4, 6]))
+        else:  # 1-4 input channels
+            c, k, m = int(rng.integers(1, 5)), int(rng.integers(1, 97)), 2
+        n = int(rng.integers(1, 3))
+        h, w = int(rng.integers(1, 25)), int(rng.integers(1, 25))
+        extra = int(rng.choice([0, 0, cwg.NO_SPLIT, cwg.FORCE_FFMA]))
+        cases.append((n, c, k, h, w, m, bf16, bool(rng.random() < 0.5), bool(rng.random() < 0.7), extra))
+    return cases
+
+
+@pytest.mark.parametrize("case", _random_cases(24), ids=lambda c: "x".join(map(str, c[:7])))
+def test_random_layers(cuda_dev, case):
+    """A seeded sweep of layer shapes against the oracle (fp32: the reference C for
+    F(2,3), the C restatement for F(4,3)/F(6,3); bf16: fp64 direct convolution of
+    the bf16-rounded operands)."""
+    n, c, k, h, w, m, bf16, relu, use_bias, extra = case
+    rng = np.random.default_rng(abs(hash(case)) % 2 ** 32)
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    g = rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32) if use_bias else None
+    flags = extra | (cwg.RELU if relu else 0)
+    if bf16:
+        x, g = workloads.bf16_round(x), workloads.bf16_round(g)
+        y = gpu_conv(x, g, bias, m, flags | cwg.BF16, cuda_dev)
+        assert_close(y, oracle.direct_conv_f64(x, g, bias, relu), "bf16", str(case))
+    else:
+        y = gpu_conv(x, g, bias, m, flags, cuda_dev)
+        assert_close(y, oracle_conv(x, g, bias, m, relu), {2: "f23", 4: "f43", 6: "f63"}[m],
+                     str(case))
+
+
 def test_bounded_wait_times_out_and_context_survives(cuda_dev):
     """A device wait on a barrier nothing arrives on gives up after its limit, the host
     reads CWG_ETIMEOUT, the status clears, and the next layer runs normally."""
