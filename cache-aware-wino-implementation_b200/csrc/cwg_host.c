@@ -211,7 +211,7 @@ static const ffma_cost kFfmaCost[] = {
     {2, 16, 1.8, 0.92}, {2, 32, 2.1, 1.10}, {2, 64, 2.5, 1.66}, {4, 16, 4.3, 1.95},
     {4, 32, 4.5, 2.56}, {4, 64, 6.3, 4.27}, {6, 16, 6.0, 4.6},
 };
-#define FFMA_SPLIT_US 2.4
+#define FFMA_SPLIT_US 4.5
 #define FFMA_RELU_PASS_US 3.5
 
 /* Picks the FFMA configuration for a layer (index into the shim's table) and its
