@@ -230,7 +230,7 @@ static int pick_ffma(int n, int c_in, int c_out, int h, int w, int m, unsigned f
   const int sms = num_sms();
   const long long th = (h + m - 1) / m, tw = (w + m - 1) / m;
   if (slices_out) *slices_out = 1;
-  if (c_out >= 32) {
+  if (c_out >= 32 && n <= 65535) { /* the kernel's grid.z holds the images */
     cwgk_ffma_cfg c;
     const int idx = find_ffma_ty(m, 32, 8, &c);
     if (idx >= 0) {

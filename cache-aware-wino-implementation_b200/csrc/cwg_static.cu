@@ -27,6 +27,9 @@ std::mutex g_ws_mu;
 
 // The host-side name g_static_ws is only a stand-in: the device address must
 // come from cudaGetSymbolAddress, once per device, with that device current.
+// The address is cached for the life of the process: a device reset
+// (cudaDeviceReset) after the first call is not supported, since the module
+// and its array would be loaded again elsewhere.
 int static_workspace(void **out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -55,12 +58,25 @@ extern "C" int cwg_conv3x3_fused_host_static(const void *x_host, const void *U,
                                              const float *bias, void *y_host, int n, int c_in,
                                              int c_out, int h, int w, int m, unsigned flags,
                                              void *stream) {
+  if (n == 0 && c_in > 0 && c_out > 0 && h > 0 && w > 0) return CWG_OK;  // empty batch
   const size_t need = cwg_host_workspace_bytes(n, c_in, c_out, h, w, flags);
   if (need == 0 || !x_host || !y_host) return CWG_EINVAL;
   if (need > (size_t)CWG_STATIC_WORKSPACE_BYTES) return CWG_EUNSUPPORTED;
   void *ws = nullptr;
   const int rc = static_workspace(&ws);
   if (rc != CWG_OK) return rc;
+  // The array used is the current device's: a stream of another device could
+  // not reach it.
+  if (stream) {
+    int sdev = -1, dev = -1;
+    cudaError_t e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev);
+    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+      cwgk_set_cuda_error((int)e);
+      return CWG_ECUDA;
+    }
+    if (sdev != dev) return CWG_EINVAL;
+  }
   // x and y are overwritten in full by the copy-in and by the kernel, so the
   // previous call's contents never leak into this one.  One stream, nothing
   // created or allocated.

@@ -1,10 +1,11 @@
 """3x3 convolution shapes of the models the reference's end-to-end driver feeds, and a
 chained runner that pushes their stride-1 layers through cwg_conv3x3_fused.
 
-The reference extracts the shapes with forward hooks on torchvision resnet18, resnet34 and
-vgg16 at a 1x3x224x224 input (benchmarks/e2e_benchmark.py:91-137) and times each layer in a
+The reference extracts the shapes with forward hooks on torchvision alexnet, resnet18, resnet34
+and vgg16 at a 1x3x224x224 input (benchmarks/e2e_benchmark.py:64, 91-137) and times each layer in a
 per-layer loop (:206-270).  Here the shapes are written out from the architectures (ResNet
-basic blocks with a stride-2 first conv in stages 2-4; VGG16 configuration D), so the engine
+basic blocks with a stride-2 first conv in stages 2-4; VGG16 configuration D; AlexNet's three
+3x3 convs after its 11x11 stride-4 and 5x5 layers and two max-pools, at 13x13), so the engine
 needs no model library; tests/test_model_shapes.py checks them against torchvision's hooks
 where torchvision is installed.  The layer ABI is stride 1, pad 1: stride-2 convs are listed
 (as the reference lists them) and skipped by the runner.
@@ -50,11 +51,20 @@ def _vgg16() -> list[ConvShape]:
     return out
 
 
+def _alexnet() -> list[ConvShape]:
+    # 224 -> conv 11x11/4, pad 2: 55 -> max-pool 3/2: 27 -> conv 5x5: 27 -> max-pool: 13
+    return [ConvShape(192, 384, 13, 13, 1), ConvShape(384, 256, 13, 13, 1),
+            ConvShape(256, 256, 13, 13, 1)]
+
+
 MODELS = {
+    "alexnet": _alexnet,
     "resnet18": lambda: _resnet((2, 2, 2, 2)),
     "resnet34": lambda: _resnet((3, 4, 6, 3)),
     "vgg16": _vgg16,
 }
+# seed offsets per model (fixed, so that adding a model changes no other model's data)
+_MODEL_ID = {"resnet18": 0, "resnet34": 1, "vgg16": 2, "alexnet": 3}
 
 
 def conv3x3_layers(name: str) -> list[ConvShape]:
@@ -70,7 +80,7 @@ def stride1_layers(name: str) -> list[ConvShape]:
 def layer_params(name: str, index: int, s: ConvShape, bf16: bool = False):
     """Seeded Kaiming-normal weights N(0, sqrt(2/(9 C_in))) and bias U(-0.1, 0.1) (BN
     folded), as for the ResNet-18 stack of the benchmark configurations."""
-    seed = 7000 + 100 * sorted(MODELS).index(name) + index
+    seed = 7000 + 100 * _MODEL_ID[name] + index
     rng = np.random.default_rng(seed)
     g = rng.normal(0.0, np.sqrt(2.0 / (9 * s.c_in)), (s.c_out, s.c_in, 3, 3)).astype(np.float32)
     bias = rng.uniform(-0.1, 0.1, s.c_out).astype(np.float32)
@@ -82,7 +92,7 @@ def layer_params(name: str, index: int, s: ConvShape, bf16: bool = False):
 
 def stack_input(name: str, index: int, n: int, s: ConvShape, bf16: bool = False) -> np.ndarray:
     """A fresh U(-1, 1) input for a layer that does not chain from its predecessor."""
-    rng = np.random.default_rng(9000 + 100 * sorted(MODELS).index(name) + index)
+    rng = np.random.default_rng(9000 + 100 * _MODEL_ID[name] + index)
     x = rng.uniform(-1.0, 1.0, (n, s.c_in, s.h, s.w)).astype(np.float32)
     if bf16:
         from workloads import bf16_round

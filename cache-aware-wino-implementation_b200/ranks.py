@@ -1,10 +1,12 @@
 """Process-per-GPU plumbing for batch-split runs (no collective on the data path).
 
-Each rank convolves its own contiguous shard of the global batch with its own
-copy of the transformed weights; the only collectives are host-side
-bookkeeping outside the timed region: a barrier, the max of per-rank device
-times, and a gather of per-rank output checksums for verification.  Backend:
-NCCL for CUDA tensors, gloo for CPU (tests).
+The batch N of a layer is split across the ranks (shard(): N / world images
+each, contiguous); each rank convolves its shard with its own copy of the
+transformed weights.  The only collectives are bookkeeping outside the timed
+region: a barrier, the max of per-rank device times, and gathers of sampled
+output images to rank 0 for verification.  This replaces the reference's
+thread fan-out of tile tasks (multicore_scheduler.py:33-50).  Backend: NCCL
+for CUDA tensors, gloo for CPU (tests).
 """
 from __future__ import annotations
 
@@ -80,6 +82,20 @@ def gather_floats(value: float, r: Rank, device=None) -> list[float]:
     out = [torch.zeros_like(t) for _ in range(r.world)]
     dist.all_gather(out, t)
     return [float(x.item()) for x in out]
+
+
+def gather_tensor(t, r: Rank) -> list:
+    """Every rank's copy of `t` (same shape and dtype on every rank), in rank order.
+    Used outside timed regions only, to bring sampled outputs to rank 0 for
+    verification; NCCL for CUDA tensors, gloo for CPU tensors."""
+    if r.world <= 1:
+        return [t]
+    import torch
+    import torch.distributed as dist
+
+    out = [torch.empty_like(t) for _ in range(r.world)]
+    dist.all_gather(out, t.contiguous())
+    return out
 
 
 def finish(r: Rank) -> None:

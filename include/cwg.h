@@ -151,7 +151,9 @@ int cwg_conv3x3_fused_host(const void *x_host, const void *U, const float *bias,
  * call on a device looks up the array's device address (cudaGetSymbolAddress);
  * make that first call before any stream capture.  All calls share the one
  * array: calls whose work overlaps on the GPU (different streams or threads
- * without ordering) race on it. */
+ * without ordering) race on it.  `stream` must belong to the current device
+ * (CWG_EINVAL otherwise); n == 0 returns CWG_OK; a device reset after the
+ * first call on that device is not supported. */
 #define CWG_STATIC_WORKSPACE_BYTES (32u << 20)
 int cwg_conv3x3_fused_host_static(const void *x_host, const void *U, const float *bias,
                                   void *y_host, int n, int c_in, int c_out, int h, int w, int m,

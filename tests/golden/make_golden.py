@@ -1,9 +1,9 @@
 """Generates the golden vectors under tests/golden/ from the reference itself.
 
-Run in a container that holds the reference project (default path below, or
-``CWG_REFERENCE``) after ``make -C oracle``:
+Run where the reference project's source tree is available, after
+``make -C oracle REF=<tree>``, naming the tree in ``CWG_REFERENCE`` (required):
 
-    python tests/golden/make_golden.py
+    CWG_REFERENCE=<path to the reference tree> python tests/golden/make_golden.py
 
 Sources of truth:
 * ``run_fused`` / ``run_non_fused`` of the reference's Python kernel
@@ -27,7 +27,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("CWG_REFERENCE", "/root/reference")
+REF = os.environ.get("CWG_REFERENCE", "")
 
 G = {
     4: np.array([[1, 0, 0], [.5, .5, .5], [.5, -.5, .5], [0, 0, 1]]),
@@ -81,6 +81,8 @@ def layer_via_run_fused(kernel, x, U, bias, td, relu):
 
 
 def main() -> None:
+    if not REF or not os.path.exists(os.path.join(REF, "src", "fused_winograd_kernel.py")):
+        raise SystemExit("set CWG_REFERENCE to the reference project's source tree")
     sys.path.insert(0, REF)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from src.fused_winograd_kernel import FusedWinogradKernel  # the reference

@@ -1,4 +1,4 @@
-"""The model shape tables (stride-1 3x3 convs of resnet18 / resnet34 / vgg16 at 224x224)
+"""The model shape tables (3x3 convs of alexnet / resnet18 / resnet34 / vgg16 at 224x224)
 against torchvision's own modules, as the reference extracts them with forward hooks
 (benchmarks/e2e_benchmark.py:91-137)."""
 import pytest
@@ -31,8 +31,8 @@ def test_tables_match_torchvision(name):
 
 
 def test_stride1_counts_and_chaining():
-    assert [len(model_shapes.stride1_layers(m)) for m in ("resnet18", "resnet34", "vgg16")] == \
-        [13, 29, 13]
+    assert [len(model_shapes.stride1_layers(m))
+            for m in ("alexnet", "resnet18", "resnet34", "vgg16")] == [3, 13, 29, 13]
     layers = model_shapes.stride1_layers("vgg16")
     assert all(model_shapes.chains(a, b) == ((a.h, a.c_out) == (b.h, b.c_in))
                for a, b in zip(layers, layers[1:]))

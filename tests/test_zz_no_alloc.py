@@ -6,8 +6,10 @@ only pass host buffers and a stream, and real-time paths that may not allocate
 after start-up cannot provide one; cwg_conv3x3_fused_host_static stages through
 a fixed array inside the library instead.  This test calls it through the C ABI
 twice in a row (different layers, so stale contents of the shared array would
-show) and compares each result with the workspace entry point's.  The file is
-named to be collected last.
+show) and compares each result with the workspace entry point's; a repeated call
+leaves the device's free memory where it was, and a call on a non-blocking
+stream of the current device gives the same result.  The file is named to be
+collected last.
 """
 import ctypes
 
@@ -63,6 +65,18 @@ def test_static_entry_matches_workspace_entry(cuda_dev):
                                n, c, k, h, w, m, flags)
         assert_close(y_static, y_ws, "f23" if m == 2 else "f43", f"static entry, seed {seed}")
 
+    # the same layer again, on a non-blocking stream: nothing allocated on the device
+    stream = torch.cuda.Stream(cuda_dev)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(cuda_dev)[0]
+    y_again = np.full((n, k, h, w), np.nan, np.float32)
+    rc = fn(x.ctypes.data, U.data_ptr(), b.data_ptr(), y_again.ctypes.data,
+            n, c, k, h, w, m, flags, stream.cuda_stream)
+    assert rc == cwg.OK, cwg.strerror(rc)
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(cuda_dev)[0] >= free0
+    assert_close(y_again, y_ws, "f23" if m == 2 else "f43", "static entry, non-blocking stream")
+
 
 def test_static_entry_rejects_layers_beyond_its_array(cuda_dev):
     fn = _static_entry()
@@ -72,3 +86,5 @@ def test_static_entry_rejects_layers_beyond_its_array(cuda_dev):
     y = np.zeros(1, np.float32)
     rc = fn(x.ctypes.data, 0x1000, None, y.ctypes.data, n, c, k, h, w, 2, 0, None)
     assert rc == cwg.EUNSUPPORTED
+    # an empty batch is a no-op, as for the device-pointer call
+    assert fn(x.ctypes.data, 0x1000, None, y.ctypes.data, 0, c, k, h, w, 2, 0, None) == cwg.OK
