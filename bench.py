@@ -787,7 +787,7 @@ def main() -> None:
     peaks, peak_src = load_peaks()
 
     r = bench_layer(layer, args, rk, dev, peaks, peak_src, steps=args.steps,
-                    warmup=args.warmup)
+                    warmup=args.warmup, extra_flags=args.flags)
     extra = []
     default_run = (args.config == 3 and args.n == 0 and not args.nonfused and not args.flags
                    and not args.weak)

@@ -48,6 +48,7 @@ const char *cwg_strerror(int status) {
     case CWG_ETIMEOUT: return "device-side wait timed out";
     case CWG_ENOMEM: return "out of memory";
     case CWG_ENODEV: return "no usable sm_100 device";
+    case CWG_ERANGE: return "an operand left the range of the kernel's fp16 arithmetic";
     default: return "unknown status";
   }
 }
@@ -88,14 +89,19 @@ static int tc_variant(unsigned flags, int m, int c_out) {
   return (m == 2 && c_out <= 64) ? CWGK_TC_PAIR64 : CWGK_TC_PAIR;
 }
 
-/* Products per multiply-accumulate on the tensor cores: 3 (bf16 hi/lo split,
- * fp32-accurate) for fp32 layers and for bf16 F(4,3) layers -- F(4,3)'s output
- * transform (coefficients up to 8) turns single bf16 products into ~6% errors
- * -- and 1 for bf16 F(2,3) layers or when CWG_TC_SINGLE asks for it. */
-static int tc_x3(int m, unsigned flags) {
-  if (flags & CWG_TC_SINGLE) return 0;
-  if (flags & CWG_BF16) return m == 4;
-  return 1;
+/* Products per multiply-accumulate on the tensor cores:
+ *   3  bf16 hi/lo split, fp32-accurate: fp32 layers (and bf16 F(4,3) layers
+ *      with CWG_TC_X3);
+ *   2  fp16 operands with V split into hi + lo: bf16 F(4,3) layers.  F(4,3)'s
+ *      output transform (coefficients up to 8) turns single bf16 products into
+ *      ~6% errors; fp16's 11 significant bits bring two products to ~5e-3
+ *      normwise against a direct convolution, at two thirds of the MMAs and half
+ *      the weight stream of the split;
+ *   1  bf16 F(2,3) layers, or when CWG_TC_SINGLE asks for it. */
+static int tc_products(int m, unsigned flags) {
+  if (flags & CWG_TC_SINGLE) return 1;
+  if (flags & CWG_BF16) return m == 4 ? ((flags & CWG_TC_X3) ? 3 : 2) : 1;
+  return 3;
 }
 
 /* F(4,3) runs on the tensor cores for bf16 layers only: with fp32 data the
@@ -104,7 +110,7 @@ static int tc_x3(int m, unsigned flags) {
 static int tc_available(int m, unsigned flags, int c_out) {
   cwgk_tc_cfg cfg;
   if (m == 4 && !(flags & CWG_BF16)) return 0;
-  return cwgk_tc_get_cfg(tc_x3(m, flags), tc_variant(flags, m, c_out), m, &cfg) == 0;
+  return cwgk_tc_get_cfg(tc_products(m, flags), tc_variant(flags, m, c_out), m, &cfg) == 0;
 }
 
 /* Tensor cores only where the per-frequency GEMM is a real contraction: both
@@ -143,8 +149,9 @@ static int decide(int c_in, int c_out, int m, unsigned flags, int *m_out, int *p
 
 static int layout_of(int path, int m, unsigned flags, int c_out) {
   if (path == CWG_PATH_TC) {
-    const int x3 = tc_x3(m, flags);
+    const int pm = tc_products(m, flags), x3 = pm == 3;
     const int v = tc_variant(flags, m, c_out);
+    if (v == CWGK_TC_PAIR && pm == 2) return CWGK_LAYOUT_TC2_H2;
     if (v == CWGK_TC_PAIR) return x3 ? CWGK_LAYOUT_TC2_X3 : CWGK_LAYOUT_TC2_X1;
     if (v == CWGK_TC_PAIR64) return x3 ? CWGK_LAYOUT_TC2H_X3 : CWGK_LAYOUT_TC2H_X1;
     return x3 ? CWGK_LAYOUT_TC_X3 : CWGK_LAYOUT_TC_X1;
@@ -163,13 +170,15 @@ static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
     case CWGK_LAYOUT_TC2_X3:
     case CWGK_LAYOUT_TC2_X1:
     case CWGK_LAYOUT_TC2H_X3:
-    case CWGK_LAYOUT_TC2H_X1: {
+    case CWGK_LAYOUT_TC2H_X1:
+    case CWGK_LAYOUT_TC2_H2: {
       /* [ceil(C_out / kb)][sets][C_pad / 16][nf][parts] blocks of `rows` rows x
        * 16 channels (rows x 32 bytes).  Pair layouts: one set per rank, and a
        * block's rows are m/2 output rows x kb = rows / (m/2) channels; 128 rows,
        * or 64 for the 64-channel pair kernel. */
       const int half = layout == CWGK_LAYOUT_TC2H_X3 || layout == CWGK_LAYOUT_TC2H_X1;
-      const int pair = half || layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
+      const int pair = half || layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1 ||
+                       layout == CWGK_LAYOUT_TC2_H2;
       const size_t rows = half ? 64 : 128;
       const size_t kb = pair ? rows / (size_t)(m / 2) : 128;
       const size_t nkb = ((size_t)c_out + kb - 1) / kb;
@@ -301,8 +310,8 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
                    4.0 * c_out;
   if (path == CWG_PATH_TC) {
     cwgk_tc_cfg t;
-    cwgk_tc_get_cfg(tc_x3(mm, flags), tc_variant(flags, mm, c_out), mm, &t);
-    out->mma_products = tc_x3(mm, flags) ? 3 : 1;
+    cwgk_tc_get_cfg(tc_products(mm, flags), tc_variant(flags, mm, c_out), mm, &t);
+    out->mma_products = tc_products(mm, flags);
     out->tiles_per_cta = t.tiles;
     out->cout_per_cta = t.kb;
     out->cin_chunk = t.cc;
@@ -316,7 +325,7 @@ int cwg_select(int n, int c_in, int c_out, int h, int w, int m, unsigned flags,
                 cwgk_tc_splits(n, c_in, c_out, h, w, mm, v, bf, split, num_sms());
     out->ctas_launched = out->ctas;
     out->order = CWG_ORDER_GRID;
-    if (n > 0 && cwgk_tc_plan(n, c_in, c_out, h, w, mm, tc_x3(mm, flags), v, bf, split,
+    if (n > 0 && cwgk_tc_plan(n, c_in, c_out, h, w, mm, tc_products(mm, flags), v, bf, split,
                               num_sms(), &out->ctas_launched, &out->order) != 0) {
       out->ctas_launched = out->ctas;
       out->order = CWG_ORDER_GRID;
@@ -397,7 +406,7 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   const int relu = (flags & CWG_RELU) ? 1 : 0;
   const int bf16 = (flags & CWG_BF16) ? 1 : 0;
   if (path == CWG_PATH_TC) {
-    return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, mm, tc_x3(mm, flags),
+    return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, mm, tc_products(mm, flags),
                         tc_variant(flags, mm, c_out), bf16, relu, !(flags & CWG_NO_SPLIT), stream);
   }
   if (small_cin(c_in, mm))
@@ -617,7 +626,8 @@ int cwg_device_status(void *stream) {
   if (e != cudaSuccess) return cuda_fail(e);
   unsigned st = 0;
   if (cwgk_read_clear_status(&st)) return CWG_ECUDA;
-  return st ? CWG_ETIMEOUT : CWG_OK;
+  if (st & 1u) return CWG_ETIMEOUT;
+  return st ? CWG_ERANGE : CWG_OK;
 }
 
 static size_t al256(size_t b) { return (b + 255) / 256 * 256; }

@@ -20,7 +20,8 @@ enum {
   CWGK_LAYOUT_TC2_X3 = 5,    /* pair kernel: At-scaled hi+lo blocks, 2 rank sets  */
   CWGK_LAYOUT_TC2_X1 = 6,    /* pair kernel: At-scaled blocks, single product     */
   CWGK_LAYOUT_TC2H_X3 = 7,   /* 64-channel pair kernel: 64-row hi+lo blocks       */
-  CWGK_LAYOUT_TC2H_X1 = 8    /* 64-channel pair kernel: 64-row blocks, 1 product  */
+  CWGK_LAYOUT_TC2H_X1 = 8,   /* 64-channel pair kernel: 64-row blocks, 1 product  */
+  CWGK_LAYOUT_TC2_H2 = 9     /* pair kernel: At-scaled fp16 blocks (F(4,3), bf16) */
 };
 
 /* Tensor-core kernel variants. */
@@ -55,7 +56,8 @@ typedef struct cwgk_tc_cfg {
 
 int cwgk_ffma_num_cfgs(void);
 int cwgk_ffma_get_cfg(int idx, cwgk_ffma_cfg *out);
-int cwgk_tc_get_cfg(int x3, int variant, int m, cwgk_tc_cfg *out);
+/* pm: products per multiply-accumulate (1 bf16, 2 fp16 with V split, 3 bf16 split) */
+int cwgk_tc_get_cfg(int pm, int variant, int m, cwgk_tc_cfg *out);
 
 /* g (or U_ref when from_ref) -> U in `layout`.  Device pointers. */
 int cwgk_weight_transform(const float *src, void *U, int c_in, int c_out, int m, int layout,
@@ -87,7 +89,7 @@ int cwgk_bias_relu(float *y, const float *bias, int n, int c_out, int h, int w, 
  * the C_in reduction of small fp32 layers across CTAs (y zeroed, partial sums
  * added atomically, bias and ReLU in a second pass). */
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
-                 int c_out, int h, int w, int m, int x3, int variant, int bf16, int relu,
+                 int c_out, int h, int w, int m, int pm, int variant, int bf16, int relu,
                  int allow_split, void *stream);
 
 /* C_in slices the tensor-core path uses for this layer (1 = no split). */
@@ -95,8 +97,19 @@ int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant,
                    int allow_split, int sms);
 /* The pair kernel's launch plan for a layer on the current device (or, without
  * one, `sms` SMs): CTAs launched and CWG_ORDER_*. */
-int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int x3, int variant, int bf16,
+int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int pm, int variant, int bf16,
                  int allow_split, int sms, long long *ctas, int *order);
+
+/* Non-fused ablation on the tensor cores.  Bytes of one operand in UMMA blocks of
+ * 128 rows x 16 channels, hi and lo bf16 (rows = output channels or tiles). */
+size_t cwgk_gemm_blocks_bytes(int nf, int rows, int c_in);
+/* U (CUDA-core layout, fp32 [nf][C][K]) -> Ug blocks, and the input pass x -> V = Bt d B
+ * in Vg blocks (nf = (m+2)^2 frequencies, T = n ceil(h/m) ceil(w/m) tiles). */
+int cwgk_gemm_prepare(const float *U, void *Ug, const float *x, void *Vg, int m, int n, int c_in,
+                      int c_out, int h, int w, void *stream);
+/* M[f][k][t] = sum_c U_f[k][c] V_f[c][t] (fp32 out) with three bf16 products per MAC. */
+int cwgk_gemm_x3(const void *Ug, const void *Vg, float *Mf, int nf, int c_in, int c_out, int T,
+                 void *stream);
 
 /* Per-tile kernel on device buffers (reference layouts). */
 int cwgk_tiles(const float *tiles, const float *U, float *out, int n_tiles, int c_in, int c_out,
@@ -108,7 +121,8 @@ int cwgh_conv_host_serial(const void *x_host, const void *U, const float *bias, 
                           char *xd, char *yd, size_t xbytes, size_t ybytes, int n, int c_in,
                           int c_out, int h, int w, int m, unsigned flags, void *stream);
 
-/* Reads and clears the device status word (after the caller synchronised). */
+/* Reads and clears the device status word (after the caller synchronised):
+ * bit 0 a bounded wait gave up, bit 1 an fp16 operand left fp16's range. */
 int cwgk_read_clear_status(unsigned *status);
 
 /* Launch counter shared by all translation units. */

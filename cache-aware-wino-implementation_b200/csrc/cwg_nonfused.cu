@@ -4,14 +4,17 @@
 // The reference's run_non_fused (src/fused_winograd_kernel.py:116-151) computes the
 // same per-tile math as run_fused; its "non-fused" difference is only logged metadata.
 // Here the three stages really are separate kernels with HBM round trips between them:
-//   1. input transform  x -> V[td^2][C][T]          (fp32, one thread per (c, tile))
-//   2. per-frequency GEMM M_f = U_f^T V_f -> M[td^2][K][T]  (cuBLAS SGEMM, strided batch)
+//   1. input transform  x -> V (one thread per (channel, tile))
+//   2. per-frequency GEMM M_f = U_f V_f -> M[td^2][K][T]  (fp32 results)
 //   3. output transform M -> y, bias, ReLU           (one thread per (k, tile))
-// T = n * ceil(h/m) * ceil(w/m).  fp32 only; U in the FFMA layout [td^2][C][K].
-#include <cublas_v2.h>
-
-#include <mutex>
-
+// T = n * ceil(h/m) * ceil(w/m).  The GEMM runs the same arithmetic as the fused
+// kernel of the same layer, so that the two differ only in fusion:
+//   F(2,3): tcgen05 MMAs with the bf16 hi/lo split (three products), as the fused
+//           pair kernel; V goes to HBM as UMMA blocks (hi and lo bf16, 4 bytes per
+//           element like fp32) and U is re-laid into such blocks by a small pass;
+//   F(4,3), F(6,3): fp32 FFMA (the fused path of fp32 layers of these sizes is the
+//           CUDA-core kernel), V fp32 [td^2][C][T].
+// fp32 only; U in the CUDA-core layout [td^2][C][K].
 #include "../../include/cwg.h"
 #include "cwg_common.cuh"
 
@@ -79,23 +82,61 @@ __global__ void output_pass(const float *__restrict__ Mf, const float *__restric
     }
 }
 
-// One cuBLAS handle per device, created on first use (plain FP32 math: no TF32).
-constexpr int kMaxDevices = 64;
-cublasHandle_t g_handle[kMaxDevices];
-std::mutex g_mu;
-
-cublasHandle_t handle_for(int dev) {
-  std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_handle[dev]) {
-    cublasHandle_t h = nullptr;
-    if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) return nullptr;
-    if (cublasSetMathMode(h, CUBLAS_PEDANTIC_MATH) != CUBLAS_STATUS_SUCCESS) {
-      cublasDestroy(h);
-      return nullptr;
+// M_f[k][t] = sum_c U_f[c][k] V_f[c][t], fp32 FFMA: a CTA computes 64 channels x
+// 128 tiles of one frequency through shared-memory tiles of 16 input channels; a
+// thread accumulates 4 channels x 8 tiles in registers.
+constexpr int kGk = 64, kGt = 128, kGc = 16;
+__global__ void __launch_bounds__(256)
+    gemm_freq_ffma(const float *__restrict__ U, const float *__restrict__ V, float *__restrict__ Mf,
+                   int C, int K, int T) {
+  __shared__ float As[kGc][kGk];
+  __shared__ float Bs[kGc][kGt];
+  const int f = blockIdx.z;
+  const int k0 = blockIdx.y * kGk, t0 = blockIdx.x * kGt;
+  const float *Uf = U + (size_t)f * C * K;
+  const float *Vf = V + (size_t)f * C * T;
+  const int tid = threadIdx.x;
+  const int tk = (tid / 16) * 4, tt = (tid % 16) * 8;
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  for (int c0 = 0; c0 < C; c0 += kGc) {
+#pragma unroll
+    for (int r = 0; r < kGc * kGk / 256; ++r) {
+      const int e = tid + r * 256, c = e / kGk, k = e % kGk;
+      As[c][k] = (c0 + c < C && k0 + k < K) ? Uf[(size_t)(c0 + c) * K + k0 + k] : 0.f;
     }
-    g_handle[dev] = h;
+#pragma unroll
+    for (int r = 0; r < kGc * kGt / 256; ++r) {
+      const int e = tid + r * 256, c = e / kGt, t = e % kGt;
+      Bs[c][t] = (c0 + c < C && t0 + t < T) ? Vf[(size_t)(c0 + c) * T + t0 + t] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < kGc; ++c) {
+      float a[4], b[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[c][tk + i];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = Bs[c][tt + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
   }
-  return g_handle[dev];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int k = k0 + tk + i;
+    if (k >= K) continue;
+    float *row = Mf + ((size_t)f * K + k) * T;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (t0 + tt + j < T) row[t0 + tt + j] = acc[i][j];
+  }
 }
 
 }  // namespace nonfused
@@ -105,12 +146,29 @@ using namespace cwg;
 
 static size_t al256(size_t b) { return (b + 255) / 256 * 256; }
 
+// Workspace: [U blocks (F(2,3))][V][M], each 256-byte aligned.
+static void nonfused_parts(int n, int c_in, int c_out, int h, int w, int m, size_t *ub,
+                           size_t *vb, size_t *mb) {
+  const size_t T = (size_t)n * ((h + m - 1) / m) * ((w + m - 1) / m);
+  const int nf = (m + 2) * (m + 2);
+  if (m == 2) {
+    *ub = al256(cwgk_gemm_blocks_bytes(nf, c_out, c_in));
+    *vb = al256(cwgk_gemm_blocks_bytes(nf, (int)T, c_in));
+  } else {
+    *ub = 0;
+    *vb = al256((size_t)nf * c_in * T * 4);
+  }
+  *mb = al256((size_t)nf * c_out * T * 4);
+}
+
 extern "C" size_t cwg_nonfused_workspace_bytes(int n, int c_in, int c_out, int h, int w, int m) {
   if (n <= 0 || c_in <= 0 || c_out <= 0 || h <= 0 || w <= 0 || (m != 2 && m != 4 && m != 6))
     return 0;
   const size_t T = (size_t)n * ((h + m - 1) / m) * ((w + m - 1) / m);
-  const size_t nf = (size_t)(m + 2) * (m + 2);
-  return al256(nf * c_in * T * 4) + al256(nf * c_out * T * 4);
+  if (T > 0x7fffff00u) return 0;
+  size_t ub, vb, mb;
+  nonfused_parts(n, c_in, c_out, h, w, m, &ub, &vb, &mb);
+  return ub + vb + mb;
 }
 
 extern "C" int cwg_conv3x3_nonfused(const float *x, const float *U, const float *bias, float *y,
@@ -127,41 +185,38 @@ extern "C" int cwg_conv3x3_nonfused(const float *x, const float *U, const float 
   const int tiles_y = (h + m - 1) / m, tiles_x = (w + m - 1) / m;
   const long long T = (long long)n * tiles_y * tiles_x;
   const int nf = (m + 2) * (m + 2);
-  if (T > 0x7fffffffLL) return CWG_EUNSUPPORTED;
-  float *V = static_cast<float *>(workspace);
-  float *Mf = reinterpret_cast<float *>(static_cast<char *>(workspace) +
-                                        al256((size_t)nf * c_in * T * 4));
+  size_t ub, vb, mb;
+  nonfused_parts(n, c_in, c_out, h, w, m, &ub, &vb, &mb);
+  char *ws = static_cast<char *>(workspace);
+  void *Ug = ws;
+  void *V = ws + ub;
+  float *Mf = reinterpret_cast<float *>(ws + ub + vb);
   cudaStream_t s = (cudaStream_t)stream;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= nonfused::kMaxDevices) {
-    cwgk_set_cuda_error((int)e);
-    return CWG_ECUDA;
-  }
-  cublasHandle_t hb = nonfused::handle_for(dev);
-  if (!hb) return CWG_ECUDA;
+  cudaError_t e;
   const int threads = 256;
-  const unsigned bx = (unsigned)(((long long)c_in * T + threads - 1) / threads);
-  if (m == 2)
-    nonfused::input_pass<2><<<bx, threads, 0, s>>>(x, V, c_in, h, w, tiles_y, tiles_x, T);
-  else if (m == 4)
-    nonfused::input_pass<4><<<bx, threads, 0, s>>>(x, V, c_in, h, w, tiles_y, tiles_x, T);
-  else
-    nonfused::input_pass<6><<<bx, threads, 0, s>>>(x, V, c_in, h, w, tiles_y, tiles_x, T);
-  cwgk_count_launch();
-  if ((e = cudaGetLastError()) != cudaSuccess) {
-    cwgk_set_cuda_error((int)e);
-    return CWG_ECUDA;
+  if (m == 2) {
+    int rc = cwgk_gemm_prepare(U, Ug, x, V, m, n, c_in, c_out, h, w, stream);
+    if (rc == 0) rc = cwgk_gemm_x3(Ug, V, Mf, nf, c_in, c_out, (int)T, stream);
+    if (rc != 0) return rc == -2 ? CWG_EUNSUPPORTED : CWG_ECUDA;
+  } else {
+    float *Vf = static_cast<float *>(V);
+    const unsigned bx = (unsigned)(((long long)c_in * T + threads - 1) / threads);
+    if (m == 4)
+      nonfused::input_pass<4><<<bx, threads, 0, s>>>(x, Vf, c_in, h, w, tiles_y, tiles_x, T);
+    else
+      nonfused::input_pass<6><<<bx, threads, 0, s>>>(x, Vf, c_in, h, w, tiles_y, tiles_x, T);
+    cwgk_count_launch();
+    const long long gt = (T + nonfused::kGt - 1) / nonfused::kGt;
+    const int gk = (c_out + nonfused::kGk - 1) / nonfused::kGk;
+    if (gt > 0x7fffffffLL || gk > 65535) return CWG_EUNSUPPORTED;
+    nonfused::gemm_freq_ffma<<<dim3((unsigned)gt, (unsigned)gk, (unsigned)nf), 256, 0, s>>>(
+        U, Vf, Mf, c_in, c_out, (int)T);
+    cwgk_count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) {
+      cwgk_set_cuda_error((int)e);
+      return CWG_ECUDA;
+    }
   }
-  // Row-major V_f [C][T], U_f [C][K], M_f [K][T]; in cuBLAS's column-major view
-  // M_f (T x K) = V_f (T x C) * U_f^T, with U_f stored as K x C (ld K).
-  const float one = 1.f, zero = 0.f;
-  if (cublasSetStream(hb, s) != CUBLAS_STATUS_SUCCESS ||
-      cublasSgemmStridedBatched(hb, CUBLAS_OP_N, CUBLAS_OP_T, (int)T, c_out, c_in, &one, V,
-                                (int)T, (long long)c_in * T, U, c_out, (long long)c_in * c_out,
-                                &zero, Mf, (int)T, (long long)c_out * T,
-                                nf) != CUBLAS_STATUS_SUCCESS)
-    return CWG_ECUDA;
   const unsigned by = (unsigned)(((long long)c_out * T + threads - 1) / threads);
   const int relu = (flags & CWG_RELU) ? 1 : 0;
   if (m == 2)

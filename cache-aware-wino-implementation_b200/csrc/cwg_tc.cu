@@ -31,6 +31,8 @@
 // returns, and the host reports CWG_ETIMEOUT.
 #include <cstdint>
 
+#include <cuda_fp16.h>
+
 #include "../../include/cwg.h"
 #include "cwg_common.cuh"
 
@@ -220,13 +222,14 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
   return d;                // base offset 0, legacy LBO mode, SWIZZLE_NONE
 }
 
-// Instruction descriptor: kind::f16, A = B = bf16, D = fp32, both K-major.
-__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
-  return (1u << 4)                     // D format fp32
-         | (1u << 7)                   // A format bf16
-         | (1u << 10)                  // B format bf16
-         | ((uint32_t)(n >> 3) << 17)  // N / 8
-         | ((uint32_t)(m >> 4) << 24); // M / 16
+// Instruction descriptor: kind::f16, A = B = bf16 (or both fp16), D = fp32, both
+// K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n, bool f16 = false) {
+  return (1u << 4)                         // D format fp32
+         | ((f16 ? 0u : 1u) << 7)          // A format: bf16 (1) or fp16 (0)
+         | ((f16 ? 0u : 1u) << 10)         // B format: the same as A
+         | ((uint32_t)(n >> 3) << 17)      // N / 8
+         | ((uint32_t)(m >> 4) << 24);     // M / 16
 }
 
 // Byte offset of element (row, k) inside one K-major no-swizzle operand block
@@ -761,6 +764,25 @@ __device__ __forceinline__ void ld_pair(const __nv_bfloat16 *p, bool ok, float &
   b = __uint_as_float(v & 0xFFFF0000u);
 }
 
+// Products per multiply-accumulate of the pair kernel (its PM parameter):
+//   kPmX3  bf16 operands split as hi + lo, three MMAs hi*hi + hi*lo + lo*hi:
+//          fp32-accurate (fp32 layers);
+//   kPmH2  fp16 operands, weights in one part and V split as hi + lo, two MMAs
+//          U*V_hi + U*V_lo (bf16 F(4,3) layers: fp16's 11 significant bits keep
+//          F(4,3)'s amplified rounding error near 5e-3 normwise, where single
+//          bf16 products reach ~6e-2);
+//   kPmX1  one bf16 MMA (bf16 F(2,3) layers).
+enum : int { kPmX1 = 1, kPmH2 = 2, kPmX3 = 3 };
+template <int PM>
+struct Prod {
+  static constexpr int kUParts = PM == kPmX3 ? 2 : 1;  // weight blocks per frequency
+  static constexpr int kVParts = PM == kPmX1 ? 1 : 2;  // V blocks per frequency
+  static constexpr bool kF16 = PM == kPmH2;            // fp16 rather than bf16 operands
+};
+// Largest finite fp16; bit of g_tc_status set when an fp16 operand would overflow.
+constexpr float kF16Max = 65504.f;
+constexpr unsigned kStatusRange = 2u;
+
 // Geometry of the pair kernel for F(M x M, 3x3).
 //   F(2,3): rank r holds the 128 rows (i = r, output channel), 64 tiles of V;
 //           N = 128, 4 accumulators Z[r][b] x 128 columns.
@@ -804,11 +826,14 @@ struct PairGeo {
 // (blocks of rows_cta rows x 16 channels: 4096 B, or 2048 B for HM):
 // block row il * cout_cta + k' of rank r holds At[r * rows_i + il][a] * U_ab for
 // output channel kblk * cout_cta + k' (scaling by 0, +-1, +-2, +-4, +-8 is exact
-// in bf16).  Channels past C_out / C_in are zero.
-template <int M, bool X3, bool HM>
+// in bf16 and fp16).  Channels past C_out / C_in are zero.  Parts: bf16 hi and
+// lo (kPmX3), one bf16 block (kPmX1) or one fp16 block (kPmH2).  An fp16 weight
+// beyond the fp16 range sets the range bit of the status word.
+template <int M, int PM, bool HM>
 __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__restrict__ U,
                                      int C, int K, int Cp, int Kp, int from_ref) {
   using G = PairGeo<M, HM>;
+  using P = Prod<PM>;
   constexpr int NF = G::NF, TD = G::TD;
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)Cp * Kp) return;
@@ -820,9 +845,10 @@ __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__r
 #pragma unroll
     for (int f = 0; f < NF; ++f) u[f] = 0.f;
   }
-  constexpr int parts = X3 ? 2 : 1;
+  constexpr int parts = P::kUParts;
   const int C16 = Cp / kCc;
   const int kb = k / G::kCoutCta, kr = k % G::kCoutCta;
+  float umax = 0.f;
 #pragma unroll
   for (int r = 0; r < 2; ++r)
 #pragma unroll
@@ -832,24 +858,32 @@ __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__r
 #pragma unroll
       for (int f = 0; f < NF; ++f) {
         const float s = Wino<M>::at(r * G::kRowsI + il, f / TD) * u[f];
-        const __nv_bfloat16 hi = __float2bfloat16_rn(s);
         uint8_t *b = U + ((blk0 * NF + f) * parts) * G::kBlkBytes;
-        *reinterpret_cast<__nv_bfloat16 *>(b + off) = hi;
-        if (X3)
-          *reinterpret_cast<__nv_bfloat16 *>(b + G::kBlkBytes + off) =
-              __float2bfloat16_rn(s - __bfloat162float(hi));
+        if constexpr (P::kF16) {
+          *reinterpret_cast<__half *>(b + off) = __float2half_rn(s);
+          umax = fmaxf(umax, fabsf(s));
+        } else {
+          const __nv_bfloat16 hi = __float2bfloat16_rn(s);
+          *reinterpret_cast<__nv_bfloat16 *>(b + off) = hi;
+          if (P::kUParts == 2)
+            *reinterpret_cast<__nv_bfloat16 *>(b + G::kBlkBytes + off) =
+                __float2bfloat16_rn(s - __bfloat162float(hi));
+        }
       }
     }
+  if (P::kF16 && !(umax <= kF16Max)) atomicOr(&g_tc_status, kStatusRange);
 }
 
 // Shared memory of one CTA of the pair.
-template <int M, bool X3, bool HM = false>
+template <int M, int PM, bool HM = false>
 struct PairLayout {
   using G = PairGeo<M, HM>;
-  static constexpr int kNU = G::kNU;
-  static constexpr int kParts = X3 ? 2 : 1;
-  static constexpr int kVStage = kParts * G::NF * G::kVBytes;
-  static constexpr int kUStage = kFPerU * kParts * G::kBlkBytes;
+  using P = Prod<PM>;
+  // weight stages: the one-part fp16 layout keeps the same bytes in flight with
+  // twice the stages
+  static constexpr int kNU = G::kNU * (PM == kPmH2 ? 2 : 1);
+  static constexpr int kVStage = P::kVParts * G::NF * G::kVBytes;
+  static constexpr int kUStage = kFPerU * P::kUParts * G::kBlkBytes;
   static constexpr int kVOff = 0;
   static constexpr int kUOff = kVOff + kNV * kVStage;
   static constexpr int kBarOff = kUOff + kNU * kUStage;
@@ -931,13 +965,13 @@ constexpr int kBarEpi = 2;
 // every item's epilogue, also after an abort (then only its barrier arrivals), so
 // that the named barriers match.  Not inlined: its registers stay out of the
 // transform loop, which calls it once per item.
-template <int M, bool X3, typename Tio, bool HM>
+template <int M, int PM, typename Tio, bool HM>
 __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *smem,
                                            const float *__restrict__ bias, Tio *__restrict__ y,
                                            int K, int H, int W, int tiles_y, int tiles_x,
                                            int total_tiles, int chunk, int kb_count,
                                            int relu, int split) {
-  using L = PairLayout<M, X3, HM>;
+  using L = PairLayout<M, PM, HM>;
   using G = PairGeo<M, HM>;
   constexpr int TD = G::TD, kN = G::kN, kNU = L::kNU;
   constexpr int kEpiThreads = 32 * G::kXWarps;
@@ -1114,15 +1148,15 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
   return run;
 }
 
-template <int M, bool X3, typename Tio, bool HM>
+template <int M, int PM, typename Tio, bool HM>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThreads, 1)
     wino_fused_tc_pair(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                        const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
                        int W, int tiles_y, int tiles_x, int total_tiles, int relu,
                        int cs_per_split, int split, int chunk, int kb_count) {
-  using L = PairLayout<M, X3, HM>;
+  using L = PairLayout<M, PM, HM>;
   using G = PairGeo<M, HM>;
-  constexpr int P = L::kParts, TD = G::TD, NF = G::NF;
+  constexpr int UP = L::P::kUParts, TD = G::TD, NF = G::NF;
   constexpr int kTiles = G::kTiles, kN = G::kN, kNU = L::kNU, kVBytes = G::kVBytes;
   constexpr int kXW = G::kXWarps;
   constexpr int kEpiThreads = 32 * kXW;
@@ -1196,7 +1230,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       int ui = 0, g = 0;
       for (int j = 0; ok && j < n_items; ++j) {
         const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
-        const uint32_t idesc = instr_desc(G::kMmaM, item_n(it.cnt));
+        const uint32_t idesc = instr_desc(G::kMmaM, item_n(it.cnt), L::P::kF16);
         if (j > 0) {
           // both CTAs' epilogue warps have read item j-1's accumulators
           ok = __all_sync(0xffffffffu, mbar_wait(tmem_empty, (j - 1) & 1, abort));
@@ -1222,14 +1256,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
 #pragma unroll
             for (int fi = 0; fi < kFPerU; ++fi) {
               const int f = fp * kFPerU + fi;
-              const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * P * G::kBlkBytes) >> 4);
+              const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * UP * G::kBlkBytes) >> 4);
               const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
               // accumulator Z[.][b], b = f % TD; its first term is a = 0 of stage 0
               const uint32_t d = tmem + (uint32_t)((f % TD) * kN);
               const uint32_t first = (cs > 0 || f >= TD) ? 1u : 0u;
               if (elect_one()) mma_pair_bf16(d, ah, bh, idesc, first);
-              if (X3) {
+              if (PM != kPmX1) {  // U * V_lo
                 if (elect_one()) mma_pair_bf16(d, ah, bh + kLo, idesc, 1u);
+              }
+              if (PM == kPmX3) {  // U_lo * V_hi
                 if (elect_one())
                   mma_pair_bf16(d, ah + (uint64_t)(G::kBlkBytes >> 4), bh, idesc, 1u);
               }
@@ -1283,7 +1319,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
     bool ok = true;
     for (int j = 0; ok && j < n_items; ++j) {
       const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
-      const uint8_t *ublk = U + ((size_t)it.kb * 2 + rank) * C16 * NF * P * G::kBlkBytes +
+      const uint8_t *ublk = U + ((size_t)it.kb * 2 + rank) * C16 * NF * UP * G::kBlkBytes +
                             (size_t)cs0 * kUPerStage * L::kUStage;
       for (int q = 0; q < nst * kUPerStage; ++q) {
         const int s = issued % kNU;
@@ -1311,12 +1347,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
     // ---------------- transform warps (this CTA's tiles) + epilogues ----------------
     const int tw = warp - 2;
     const int grp = tw / G::kGroupWarps, gw = tw % G::kGroupWarps;
-    // warp -> (16-tile block, 2*CPT channels); lane -> (tile, CPT channels).  A
-    // warp load reads 16 consecutive tiles of 2 channel planes.
+    // warp -> (16-tile block, K half cgrp >> 1, 4-channel quarter); lane -> (tile,
+    // CPT channels).  Lanes 0-15 (the block's tiles 0-7) and lanes 16-31 (tiles
+    // 8-15) take the two opposite quarters of the K half: B rows t and t + 8 share
+    // a bank group, so their 4-byte V stores then land on different words and a
+    // warp store fills all 32 banks once (the same quarter for all 16 tiles
+    // replayed every store).  A warp load reads 8 consecutive tiles of 4 channel
+    // planes.
     constexpr int CPT = G::kCpt;
     constexpr int kTileBlocks = kTiles / 16;
-    const int cgrp = gw / kTileBlocks;
-    const int cbase = cgrp * (2 * CPT) + (lane & 1) * CPT;
+    const int cgrp = gw / kTileBlocks;  // 0..3
+    const int cbase = (cgrp >> 1) * 8 + ((cgrp & 1) ^ (lane >> 4)) * 4 + (lane & 1) * CPT;
     const int kh = cbase >> 3;
     const int tb16 = (gw % kTileBlocks) * 16;  // first of the warp's 16 B rows
     const int t = tb16 + (lane >> 1);          // this lane's B row
@@ -1399,9 +1440,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
     };
     // V of frequency f, channels cbase .. cbase+CPT-1 of row t: 2*CPT bytes per part
     const uint32_t voff = (uint32_t)(kh * (kTiles * 16) + t * 16 + (cbase & 7) * 2);
+    float vmax = 0.f;  // largest |V| an fp16 layout stored (range check)
     auto put_v = [&](uint8_t *vb, int f, const float (&e)[CPT]) {
       uint32_t hi2, lo2;
-      if (X3) {
+      if constexpr (PM == kPmH2) {
+        const __half2 h = __floats2half2_rn(e[0], e[1]);
+        const float2 hf = __half22float2(h);
+        const __half2 l = __floats2half2_rn(e[0] - hf.x, e[1] - hf.y);
+        hi2 = *reinterpret_cast<const uint32_t *>(&h);
+        lo2 = *reinterpret_cast<const uint32_t *>(&l);
+        vmax = fmaxf(vmax, fmaxf(fabsf(e[0]), fabsf(e[1])));
+        *reinterpret_cast<uint32_t *>(vb + (NF + f) * kVBytes + voff) = lo2;
+      } else if constexpr (PM == kPmX3) {
         split_pair(e[0], e[1], hi2, lo2);
         *reinterpret_cast<uint32_t *>(vb + (NF + f) * kVBytes + voff) = lo2;
       } else {
@@ -1427,7 +1477,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       // (F(2,3): stage s's patches are already in registers, their loads having
       // overlapped the last MMAs and the epilogue)
       while (ep < n_items && s > (ep + 1) * nst)
-        ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
+        ok = pair_epilogue<M, PM, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
                                            tiles_x, total_tiles, chunk, kb_count, relu, split) &&
              ok;
       if (!ok) break;
@@ -1497,10 +1547,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       }
     }
     while (ep < n_items)
-      ok = pair_epilogue<M, X3, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
+      ok = pair_epilogue<M, PM, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
                                          total_tiles, chunk, kb_count, relu, split) &&
            ok;
     if (n_items == 0) named_bar_sync(kBarTmem, 32 + kEpiThreads);
+    if constexpr (PM == kPmH2) {
+      // an input whose transform left the fp16 range made the result invalid
+      if (__any_sync(0xffffffffu, !(vmax <= kF16Max)) && lane == 0)
+        atomicOr(&g_tc_status, kStatusRange);
+    }
   }
 
   tc_fence_before();
@@ -1625,19 +1680,24 @@ static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
   constexpr double kFixed = M == 2 ? 0.5 : 0.75, kPrologue = 0.1;
   const long long blocks = (total + G::kN - 1) / G::kN, units = blocks * gy;
   PairPlan p{blocks, G::kN, gy, 1, CWG_ORDER_GRID};
-  if (splits > 1 || resident <= 0 || units <= resident) return p;
+  if (splits > 1 || resident <= 0) return p;
+  // one wave of whole units: one item per pair
+  const double grid = units <= resident ? 1.0 + kPrologue : 1e300;
   // round robin: every pair takes ceil(units / resident) whole units at most
-  const double rr = (double)((units + resident - 1) / resident) + kPrologue;
-  // equal runs of tiles: whole items plus one short item per channel block
-  double eq = 1e300;
+  const double rr = units > resident ? (double)((units + resident - 1) / resident) + kPrologue
+                                     : 1e300;
+  // equal runs of tiles over every resident pair: whole items plus one short item
+  // per channel block (a layer of less than one wave of full items then runs
+  // shorter items on more pairs: 8 images of 128->128 at 56x56, 49 blocks of 128
+  // tiles, run as 66 items of 96 tiles)
   // runs start on a multiple of 16 tiles: a lane's pixels then stay in one image
   // row and aligned for a vector store whenever the row holds an even number of tiles
   const long long chunk = ((total + resident - 1) / resident + 15) / 16 * 16;
-  if (chunk >= G::kN) {
-    const long long full = chunk / G::kN, rem = chunk % G::kN;
-    eq = (double)gy * ((double)full + (rem ? kFixed + (1 - kFixed) * (double)rem / G::kN : 0.0)) +
-         kPrologue;
-  }
+  const long long full = chunk / G::kN, rem = chunk % G::kN;
+  const double eq =
+      (double)gy * ((double)full + (rem ? kFixed + (1 - kFixed) * (double)rem / G::kN : 0.0)) +
+      kPrologue;
+  if (grid <= eq && grid <= rr) return p;
   if (eq < rr) {
     p.chunk = chunk;
     p.pairs = (total + chunk - 1) / chunk;
@@ -1652,12 +1712,12 @@ static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
   return p;
 }
 
-template <int M, bool X3, typename Tio, bool HM>
+template <int M, int PM, typename Tio, bool HM>
 static cudaError_t launch_pair(const void *x, const void *U, const float *bias, void *y, int n,
                                int c, int k, int h, int w, int relu, int allow_split,
                                cudaStream_t s) {
   using G = PairGeo<M, HM>;
-  using L = PairLayout<M, X3, HM>;
+  using L = PairLayout<M, PM, HM>;
   const int tiles_y = (h + M - 1) / M, tiles_x = (w + M - 1) / M;
   const long long total = (long long)n * tiles_y * tiles_x;
   const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
@@ -1669,11 +1729,11 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
   const int splits = (allow_split && sizeof(Tio) == 4) ? split_stages<M, HM>(n, c, k, h, w, sms / 2,
                                                                          &per)
                                                        : 1;
-  auto fn = wino_fused_tc_pair<M, X3, Tio, HM>;
-  e = smem_attr_once<wino_fused_tc_pair<M, X3, Tio, HM>>(L::kSmem);
+  auto fn = wino_fused_tc_pair<M, PM, Tio, HM>;
+  e = smem_attr_once<wino_fused_tc_pair<M, PM, Tio, HM>>(L::kSmem);
   if (e != cudaSuccess) return e;
   const int resident =
-      resident_pairs<wino_fused_tc_pair<M, X3, Tio, HM>>(G::kThreads, L::kSmem, sms);
+      resident_pairs<wino_fused_tc_pair<M, PM, Tio, HM>>(G::kThreads, L::kSmem, sms);
   const PairPlan plan = plan_pairs<M, HM>(total, gy, splits, resident);
   // tile indices, item counts and units are 32-bit in the kernel
   if (total * gy > 0x7fffffffLL || 2 * plan.pairs > 0x7fffffffLL || plan.gy > 65535)
@@ -1691,11 +1751,11 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
 
 // The launch plan of a layer as launch_pair would make it on the current device
 // (without one: `sms` SMs and one cluster per TPC).
-template <int M, bool X3, typename Tio, bool HM>
+template <int M, int PM, typename Tio, bool HM>
 static void plan_layer(int n, int c, int k, int h, int w, int allow_split, int sms,
                        long long *ctas, int *order) {
   using G = PairGeo<M, HM>;
-  using L = PairLayout<M, X3, HM>;
+  using L = PairLayout<M, PM, HM>;
   const long long total = (long long)n * ((h + M - 1) / M) * ((w + M - 1) / M);
   const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
   int per = 0;
@@ -1703,13 +1763,222 @@ static void plan_layer(int n, int c, int k, int h, int w, int allow_split, int s
       (allow_split && sizeof(Tio) == 4) ? split_stages<M, HM>(n, c, k, h, w, sms / 2, &per) : 1;
   int resident = sms / 2, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess &&
-      smem_attr_once<wino_fused_tc_pair<M, X3, Tio, HM>>(L::kSmem) == cudaSuccess)
-    resident = resident_pairs<wino_fused_tc_pair<M, X3, Tio, HM>>(G::kThreads, L::kSmem, sms);
+      smem_attr_once<wino_fused_tc_pair<M, PM, Tio, HM>>(L::kSmem) == cudaSuccess)
+    resident = resident_pairs<wino_fused_tc_pair<M, PM, Tio, HM>>(G::kThreads, L::kSmem, sms);
   else
     (void)cudaGetLastError();
   const PairPlan p = plan_pairs<M, HM>(total, gy, splits, resident);
   *ctas = 2 * p.pairs * p.gy * splits;
   *order = p.order;
+}
+
+// ==== batched per-frequency GEMM of the non-fused ablation ===========================
+//
+// M_f[k][t] = sum_c U_f[k][c] V_f[c][t] for every frequency f, fp32 results in HBM
+// ([f][K][T], t contiguous), on the tensor cores with the fp32-parity products of
+// the fused kernels (bf16 hi/lo split, three MMAs per 16-channel step).  Both
+// operands arrive in HBM as ready-made UMMA blocks of 128 rows x 16 channels
+// (the blk_off layout, hi and lo blocks adjacent):
+//   A: Ug [nf][Kp/128][C16][hi, lo][4096 B]   rows = output channels
+//   B: Vg [nf][Tp/128][C16][hi, lo][4096 B]   rows = tiles
+// One CTA per (128-tile block, 128-channel block, frequency): warp 0 owns 128
+// TMEM columns and issues the MMAs, warp 1 streams the 16 KB stages by
+// cp.async.bulk, warps 2-5 read the accumulator (lane = output channel) and
+// store rows of M.  Every wait is bounded, as in the fused kernels.
+constexpr int kGemmStages = 4;
+constexpr int kGemmStage = 4 * kCoreBytes;  // A hi, A lo, B hi, B lo
+constexpr int kGemmThreads = 6 * 32;
+constexpr int kGemmBarOff = kGemmStages * kGemmStage;
+// full[stages], empty[stages], acc_full, drain; then the TMEM slot and abort flag
+constexpr int kGemmSmem = kGemmBarOff + 8 * (2 * kGemmStages + 2) + 8;
+
+__global__ void __launch_bounds__(kGemmThreads)
+    gemm_freq_x3(const uint8_t *__restrict__ Ug, const uint8_t *__restrict__ Vg,
+                 float *__restrict__ Mf, int K, int T, int C16, int Kb, int Tb) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t full = sbase + kGemmBarOff, empty = full + 8 * kGemmStages;
+  const uint32_t acc_full = empty + 8 * kGemmStages, drain = acc_full + 8;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kGemmBarOff + 8 * (2 * kGemmStages + 2));
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  const int warp = __shfl_sync(0xffffffffu, (int)(threadIdx.x >> 5), 0);
+  const int lane = threadIdx.x & 31;
+  const int tb = blockIdx.x, kb = blockIdx.y, f = blockIdx.z;
+  const uint8_t *a_src = Ug + ((size_t)f * Kb + kb) * C16 * 2 * kCoreBytes;
+  const uint8_t *b_src = Vg + ((size_t)f * Tb + tb) * C16 * 2 * kCoreBytes;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGemmStages; ++i) {
+      mbar_init(full + 8 * i, 1);
+      mbar_init(empty + 8 * i, 1);
+    }
+    mbar_init(acc_full, 1);
+    mbar_init(drain, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(128));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    tc_fence_before();
+    __syncwarp();
+    named_bar_arrive(kBarTmem, 32 + 4 * 32);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    constexpr uint32_t idesc = instr_desc(128, 128);
+    constexpr uint64_t kBlk = (uint64_t)(kCoreBytes >> 4);
+    bool ok = true;
+    for (int cs = 0; cs < C16; ++cs) {
+      const int st = cs % kGemmStages;
+      ok = __all_sync(0xffffffffu, mbar_wait(full + 8 * st, (cs / kGemmStages) & 1, abort));
+      if (!ok) break;
+      tc_fence_after();
+      const uint64_t a = smem_desc(sbase + st * kGemmStage, 128, 256);
+      const uint64_t b = a + 2 * kBlk;
+      if (elect_one()) mma_bf16(tmem, a, b, idesc, cs > 0 ? 1u : 0u);  // hi * hi
+      if (elect_one()) mma_bf16(tmem, a, b + kBlk, idesc, 1u);         // hi * lo
+      if (elect_one()) mma_bf16(tmem, a + kBlk, b, idesc, 1u);         // lo * hi
+      __syncwarp();
+      if (elect_one()) tc_commit(empty + 8 * st);
+      __syncwarp();
+    }
+    if (ok) {
+      if (elect_one()) tc_commit(acc_full);
+      __syncwarp();
+    } else {
+      if (elect_one()) tc_commit(drain);
+      __syncwarp();
+      const unsigned long long t0 = globaltimer();
+      while (!mbar_try(drain, 0) && globaltimer() - t0 < kTimeoutNs) {
+      }
+    }
+  } else if (warp == 1) {
+    int issued = 0;
+    for (int cs = 0; cs < C16; ++cs) {
+      const int st = cs % kGemmStages;
+      if (!__all_sync(0xffffffffu,
+                      mbar_wait(empty + 8 * st, ((cs / kGemmStages) & 1) ^ 1, abort)))
+        break;
+      if (elect_one()) {
+        mbar_expect_tx(full + 8 * st, kGemmStage);
+        bulk_g2s(sbase + st * kGemmStage, a_src + (size_t)cs * 2 * kCoreBytes, 2 * kCoreBytes,
+                 full + 8 * st);
+        bulk_g2s(sbase + st * kGemmStage + 2 * kCoreBytes, b_src + (size_t)cs * 2 * kCoreBytes,
+                 2 * kCoreBytes, full + 8 * st);
+      }
+      __syncwarp();
+      issued = cs + 1;
+    }
+    // never leave the CTA with a copy still writing shared memory
+    for (int i = issued - kGemmStages > 0 ? issued - kGemmStages : 0; i < issued; ++i) {
+      const int st = i % kGemmStages;
+      const unsigned long long t0 = globaltimer();
+      while (!mbar_try(full + 8 * st, (i / kGemmStages) & 1) && globaltimer() - t0 < kTimeoutNs) {
+      }
+    }
+  } else {
+    // epilogue: TMEM lanes 32 quad .. 32 quad + 31 = output channels, columns = tiles
+    named_bar_sync(kBarTmem, 32 + 4 * 32);
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0, abort));
+    tc_fence_after();
+    if (ok) {
+      const int quad = warp & 3;
+      const int k = kb * 128 + quad * 32 + lane;
+      const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
+      float *row = Mf + ((size_t)f * K + (k < K ? k : 0)) * (size_t)T;
+      const bool vec = (T & 3) == 0 && (reinterpret_cast<uintptr_t>(Mf) & 15) == 0;
+#pragma unroll 1
+      for (int c0 = 0; c0 < 128; c0 += 8) {
+        float v[8];
+        tmem_ld8(trow + (uint32_t)c0, v);  // whole warp, converged
+        tmem_wait_ld();
+        const int t0 = tb * 128 + c0;
+        if (k < K && t0 < T) {
+          if (vec && t0 + 8 <= T) {
+            *reinterpret_cast<float4 *>(row + t0) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4 *>(row + t0 + 4) = make_float4(v[4], v[5], v[6], v[7]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (t0 + e < T) row[t0 + e] = v[e];
+          }
+        }
+        __syncwarp();
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot),
+                 "r"(128));
+  }
+}
+
+// U in the CUDA-core layout, fp32 [nf][C][K] -> Ug blocks (hi, lo); zero past C, K.
+__global__ void gemm_u_blocks(const float *__restrict__ U, uint8_t *__restrict__ Ug, int nf, int C,
+                              int K, int C16, int Kb) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long Kp = (long long)Kb * 128, Cp = (long long)C16 * 16;
+  if (idx >= (long long)nf * Cp * Kp) return;
+  const int k = (int)(idx % Kp);
+  const int c = (int)((idx / Kp) % Cp);
+  const int f = (int)(idx / (Kp * Cp));
+  const float u = (k < K && c < C) ? U[((size_t)f * C + c) * K + k] : 0.f;
+  const __nv_bfloat16 hi = __float2bfloat16_rn(u);
+  const __nv_bfloat16 lo = __float2bfloat16_rn(u - __bfloat162float(hi));
+  uint8_t *blk = Ug + ((((size_t)f * Kb + k / 128) * C16 + c / 16) * 2) * kCoreBytes;
+  const uint32_t off = blk_off(k % 128, c % 16);
+  *reinterpret_cast<__nv_bfloat16 *>(blk + off) = hi;
+  *reinterpret_cast<__nv_bfloat16 *>(blk + kCoreBytes + off) = lo;
+}
+
+// Input pass of the ablation for the tensor-core GEMM: V = Bt d B of one (channel,
+// tile) written as hi/lo bf16 into the Vg blocks; zero past C and T (the blocks
+// cover the padded ranges, so no memset is needed).
+template <int M>
+__global__ void gemm_v_blocks(const float *__restrict__ x, uint8_t *__restrict__ Vg, int C, int H,
+                              int W, int tiles_y, int tiles_x, int T, int C16, int Tb) {
+  constexpr int TD = M + 2, NF = TD * TD;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long Tp = (long long)Tb * 128, Cp = (long long)C16 * 16;
+  if (idx >= Cp * Tp) return;
+  const int t = (int)(idx % Tp);
+  const int c = (int)(idx / Tp);
+  float d[TD][TD], v[TD][TD];
+  const bool ok = t < T && c < C;
+  const int per_img = tiles_y * tiles_x;
+  const int n = ok ? t / per_img : 0;
+  const int rem = ok ? t - n * per_img : 0;
+  const int ty = rem / tiles_x, tx = rem - ty * tiles_x;
+  const int y0 = M * ty - 1, x0 = M * tx - 1;
+  const float *xc = x + ((size_t)n * C + (ok ? c : 0)) * H * W;
+#pragma unroll
+  for (int i = 0; i < TD; ++i)
+#pragma unroll
+    for (int j = 0; j < TD; ++j) {
+      const int yy = y0 + i, xx = x0 + j;
+      d[i][j] = (ok && yy >= 0 && yy < H && xx >= 0 && xx < W) ? xc[(size_t)yy * W + xx] : 0.f;
+    }
+  input_transform<M, true>(d, v);
+  const uint32_t off = blk_off(t % 128, c % 16);
+#pragma unroll
+  for (int f = 0; f < NF; ++f) {
+    const float e = v[f / TD][f % TD];
+    const __nv_bfloat16 hi = __float2bfloat16_rn(e);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(e - __bfloat162float(hi));
+    uint8_t *blk = Vg + ((((size_t)f * Tb + t / 128) * C16 + c / 16) * 2) * kCoreBytes;
+    *reinterpret_cast<__nv_bfloat16 *>(blk + off) = hi;
+    *reinterpret_cast<__nv_bfloat16 *>(blk + kCoreBytes + off) = lo;
+  }
 }
 
 // Diagnostics: one CTA waits, through the kernels' own bounded wait, on an
@@ -1735,35 +2004,40 @@ using namespace cwg;
 
 extern "C" {
 
-int cwgk_tc_get_cfg(int x3, int variant, int m, cwgk_tc_cfg *out) {
-  if (!out) return -1;
+int cwgk_tc_get_cfg(int pm, int variant, int m, cwgk_tc_cfg *out) {
+  using namespace tc;
+  if (!out || pm < kPmX1 || pm > kPmX3) return -1;
+  const bool x3 = pm == kPmX3;
   out->m = m;
   out->kb = tc::kCout;
   out->cc = tc::kCc;
   out->tmem_cols = tc::kTmemCols;
   if (variant == CWGK_TC_PAIR) {
-    if (m == 2) {
-      out->tiles = tc::PairGeo<2>::kN;
-      out->kb = tc::PairGeo<2>::kCoutCta;
-      out->threads = tc::PairGeo<2>::kThreads;
-      out->smem = x3 ? tc::PairLayout<2, true>::kSmem : tc::PairLayout<2, false>::kSmem;
+    if (m == 2 && pm != kPmH2) {  // fp16 products serve the F(4,3) layers only
+      out->tiles = PairGeo<2>::kN;
+      out->kb = PairGeo<2>::kCoutCta;
+      out->threads = PairGeo<2>::kThreads;
+      out->smem = x3 ? PairLayout<2, kPmX3>::kSmem : PairLayout<2, kPmX1>::kSmem;
     } else if (m == 4) {
-      out->tiles = tc::PairGeo<4>::kN;
-      out->kb = tc::PairGeo<4>::kCoutCta;
-      out->threads = tc::PairGeo<4>::kThreads;
-      out->smem = x3 ? tc::PairLayout<4, true>::kSmem : tc::PairLayout<4, false>::kSmem;
+      out->tiles = PairGeo<4>::kN;
+      out->kb = PairGeo<4>::kCoutCta;
+      out->threads = PairGeo<4>::kThreads;
+      out->smem = pm == kPmX3 ? PairLayout<4, kPmX3>::kSmem
+                              : (pm == kPmH2 ? PairLayout<4, kPmH2>::kSmem
+                                             : PairLayout<4, kPmX1>::kSmem);
     } else {
       return -1;
     }
     out->ctas_per_tile_block = 2;
     return 0;
   }
+  if (pm == kPmH2) return -1;
   if (variant == CWGK_TC_PAIR64) {
     if (m != 2) return -1;
-    out->tiles = tc::PairGeo<2, true>::kN;
-    out->kb = tc::PairGeo<2, true>::kCoutCta;
-    out->threads = tc::PairGeo<2, true>::kThreads;
-    out->smem = x3 ? tc::PairLayout<2, true, true>::kSmem : tc::PairLayout<2, false, true>::kSmem;
+    out->tiles = PairGeo<2, true>::kN;
+    out->kb = PairGeo<2, true>::kCoutCta;
+    out->threads = PairGeo<2, true>::kThreads;
+    out->smem = x3 ? PairLayout<2, kPmX3, true>::kSmem : PairLayout<2, kPmX1, true>::kSmem;
     out->ctas_per_tile_block = 2;
     return 0;
   }
@@ -1788,10 +2062,12 @@ int cwgk_tc_get_cfg(int x3, int variant, int m, cwgk_tc_cfg *out) {
 int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int m, int layout,
                              int from_ref, void *stream) {
   const bool half = layout == CWGK_LAYOUT_TC2H_X3 || layout == CWGK_LAYOUT_TC2H_X1;
-  const bool pair = half || layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
+  const bool h2 = layout == CWGK_LAYOUT_TC2_H2;
+  const bool pair = half || h2 || layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
   const bool x3 = layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3 ||
                   layout == CWGK_LAYOUT_TC2H_X3;
   if (!(m == 2 || (m == 4 && pair && !half))) return -2;
+  if (h2 && m != 4) return -2;
   if (!pair && layout != CWGK_LAYOUT_TC_X1 && layout != CWGK_LAYOUT_TC_X3) return -2;
   const int kb = half ? tc::PairGeo<2, true>::kCoutCta
                       : (pair ? (m == 2 ? tc::PairGeo<2>::kCoutCta : tc::PairGeo<4>::kCoutCta)
@@ -1811,19 +2087,21 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
       CWG_WT(tc::wt_transform_tc<false>);
   } else if (half) {
     if (x3)
-      CWG_WT((tc::wt_transform_tc_pair<2, true, true>));
+      CWG_WT((tc::wt_transform_tc_pair<2, tc::kPmX3, true>));
     else
-      CWG_WT((tc::wt_transform_tc_pair<2, false, true>));
+      CWG_WT((tc::wt_transform_tc_pair<2, tc::kPmX1, true>));
   } else if (m == 2) {
     if (x3)
-      CWG_WT((tc::wt_transform_tc_pair<2, true, false>));
+      CWG_WT((tc::wt_transform_tc_pair<2, tc::kPmX3, false>));
     else
-      CWG_WT((tc::wt_transform_tc_pair<2, false, false>));
+      CWG_WT((tc::wt_transform_tc_pair<2, tc::kPmX1, false>));
   } else {
     if (x3)
-      CWG_WT((tc::wt_transform_tc_pair<4, true, false>));
+      CWG_WT((tc::wt_transform_tc_pair<4, tc::kPmX3, false>));
+    else if (h2)
+      CWG_WT((tc::wt_transform_tc_pair<4, tc::kPmH2, false>));
     else
-      CWG_WT((tc::wt_transform_tc_pair<4, false, false>));
+      CWG_WT((tc::wt_transform_tc_pair<4, tc::kPmX1, false>));
   }
 #undef CWG_WT
   cwgk_count_launch();
@@ -1859,51 +2137,64 @@ int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant,
                 : tc::split_stages<4, false>(n, c_in, c_out, h, w, sms / 2, &per);
 }
 
-int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int x3, int variant, int bf16,
+int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int pm, int variant, int bf16,
                  int allow_split, int sms, long long *ctas, int *order) {
+  using namespace tc;
   if (!(variant == CWGK_TC_PAIR && (m == 2 || m == 4)) && !(variant == CWGK_TC_PAIR64 && m == 2))
     return -1;
-#define CWG_PLAN(M_, X3_, T_, HM_) \
-  tc::plan_layer<M_, X3_, T_, HM_>(n, c_in, c_out, h, w, allow_split, sms, ctas, order)
+  if (pm == kPmH2 && !(m == 4 && bf16)) return -1;
+#define CWG_PLAN(M_, PM_, T_, HM_) \
+  plan_layer<M_, PM_, T_, HM_>(n, c_in, c_out, h, w, allow_split, sms, ctas, order)
+  const bool x3 = pm == kPmX3;
   if (variant == CWGK_TC_PAIR64) {
     if (bf16)
-      x3 ? CWG_PLAN(2, true, __nv_bfloat16, true) : CWG_PLAN(2, false, __nv_bfloat16, true);
+      x3 ? CWG_PLAN(2, kPmX3, __nv_bfloat16, true) : CWG_PLAN(2, kPmX1, __nv_bfloat16, true);
     else
-      x3 ? CWG_PLAN(2, true, float, true) : CWG_PLAN(2, false, float, true);
+      x3 ? CWG_PLAN(2, kPmX3, float, true) : CWG_PLAN(2, kPmX1, float, true);
   } else if (m == 2) {
     if (bf16)
-      x3 ? CWG_PLAN(2, true, __nv_bfloat16, false) : CWG_PLAN(2, false, __nv_bfloat16, false);
+      x3 ? CWG_PLAN(2, kPmX3, __nv_bfloat16, false) : CWG_PLAN(2, kPmX1, __nv_bfloat16, false);
     else
-      x3 ? CWG_PLAN(2, true, float, false) : CWG_PLAN(2, false, float, false);
+      x3 ? CWG_PLAN(2, kPmX3, float, false) : CWG_PLAN(2, kPmX1, float, false);
+  } else if (pm == kPmH2) {
+    CWG_PLAN(4, kPmH2, __nv_bfloat16, false);
   } else {
     if (bf16)
-      x3 ? CWG_PLAN(4, true, __nv_bfloat16, false) : CWG_PLAN(4, false, __nv_bfloat16, false);
+      x3 ? CWG_PLAN(4, kPmX3, __nv_bfloat16, false) : CWG_PLAN(4, kPmX1, __nv_bfloat16, false);
     else
-      x3 ? CWG_PLAN(4, true, float, false) : CWG_PLAN(4, false, float, false);
+      x3 ? CWG_PLAN(4, kPmX3, float, false) : CWG_PLAN(4, kPmX1, float, false);
   }
 #undef CWG_PLAN
   return 0;
 }
 
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
-                 int c_out, int h, int w, int m, int x3, int variant, int bf16, int relu,
+                 int c_out, int h, int w, int m, int pm, int variant, int bf16, int relu,
                  int allow_split, void *stream) {
+  using tc::kPmH2;
+  using tc::kPmX1;
+  using tc::kPmX3;
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
+  const bool x3 = pm == kPmX3;
 #define CWG_TC_LAUNCH(X3_, HALF_)                                                              \
   (bf16 ? tc::launch<X3_, HALF_, __nv_bfloat16>(x, U, bias, y, n, c_in, c_out, h, w, relu, s) \
         : tc::launch<X3_, HALF_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
-#define CWG_TC_LAUNCH_PAIR(M_, X3_, HM_)                                                        \
-  (bf16 ? tc::launch_pair<M_, X3_, __nv_bfloat16, HM_>(x, U, bias, y, n, c_in, c_out, h, w,   \
+#define CWG_TC_LAUNCH_PAIR(M_, PM_, HM_)                                                        \
+  (bf16 ? tc::launch_pair<M_, PM_, __nv_bfloat16, HM_>(x, U, bias, y, n, c_in, c_out, h, w,   \
                                                         relu, allow_split, s)                 \
-        : tc::launch_pair<M_, X3_, float, HM_>(x, U, bias, y, n, c_in, c_out, h, w, relu,     \
+        : tc::launch_pair<M_, PM_, float, HM_>(x, U, bias, y, n, c_in, c_out, h, w, relu,     \
                                                allow_split, s))
-  if (variant == CWGK_TC_PAIR && m == 2)
-    e = x3 ? CWG_TC_LAUNCH_PAIR(2, true, false) : CWG_TC_LAUNCH_PAIR(2, false, false);
+  if (pm == kPmH2) {  // bf16 F(4,3) layers only
+    if (!(variant == CWGK_TC_PAIR && m == 4 && bf16)) return -2;
+    e = tc::launch_pair<4, kPmH2, __nv_bfloat16, false>(x, U, bias, y, n, c_in, c_out, h, w,
+                                                        relu, allow_split, s);
+  } else if (variant == CWGK_TC_PAIR && m == 2)
+    e = x3 ? CWG_TC_LAUNCH_PAIR(2, kPmX3, false) : CWG_TC_LAUNCH_PAIR(2, kPmX1, false);
   else if (variant == CWGK_TC_PAIR64 && m == 2)
-    e = x3 ? CWG_TC_LAUNCH_PAIR(2, true, true) : CWG_TC_LAUNCH_PAIR(2, false, true);
+    e = x3 ? CWG_TC_LAUNCH_PAIR(2, kPmX3, true) : CWG_TC_LAUNCH_PAIR(2, kPmX1, true);
   else if (variant == CWGK_TC_PAIR && m == 4)
-    e = x3 ? CWG_TC_LAUNCH_PAIR(4, true, false) : CWG_TC_LAUNCH_PAIR(4, false, false);
+    e = x3 ? CWG_TC_LAUNCH_PAIR(4, kPmX3, false) : CWG_TC_LAUNCH_PAIR(4, kPmX1, false);
   else if (variant == CWGK_TC_HALF && m == 2)
     e = x3 ? CWG_TC_LAUNCH(true, true) : CWG_TC_LAUNCH(false, true);
   else if (variant == CWGK_TC_FULL16 && m == 2)
@@ -1913,6 +2204,62 @@ int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n
 #undef CWG_TC_LAUNCH
 #undef CWG_TC_LAUNCH_PAIR
   cwgk_count_launch();
+  if (e != cudaSuccess) {
+    cwgk_set_cuda_error((int)e);
+    return -3;
+  }
+  return 0;
+}
+
+size_t cwgk_gemm_blocks_bytes(int nf, int rows, int c_in) {
+  return (size_t)nf * ((rows + 127) / 128) * ((c_in + 15) / 16) * 2 * tc::kCoreBytes;
+}
+
+int cwgk_gemm_prepare(const float *U, void *Ug, const float *x, void *Vg, int m, int n, int c_in,
+                      int c_out, int h, int w, void *stream) {
+  cudaStream_t s = (cudaStream_t)stream;
+  const int nf = (m + 2) * (m + 2);
+  const int tiles_y = (h + m - 1) / m, tiles_x = (w + m - 1) / m;
+  const long long T = (long long)n * tiles_y * tiles_x;
+  if (T > 0x7fffffffLL - 128) return -2;
+  const int C16 = (c_in + 15) / 16, Kb = (c_out + 127) / 128, Tb = (int)((T + 127) / 128);
+  const int threads = 256;
+  const long long nu = (long long)nf * C16 * 16 * Kb * 128;
+  tc::gemm_u_blocks<<<(unsigned)((nu + threads - 1) / threads), threads, 0, s>>>(
+      U, (uint8_t *)Ug, nf, c_in, c_out, C16, Kb);
+  cwgk_count_launch();
+  const long long nv = (long long)C16 * 16 * Tb * 128;
+  const unsigned bv = (unsigned)((nv + threads - 1) / threads);
+  if (m == 2)
+    tc::gemm_v_blocks<2><<<bv, threads, 0, s>>>(x, (uint8_t *)Vg, c_in, h, w, tiles_y, tiles_x,
+                                                 (int)T, C16, Tb);
+  else if (m == 4)
+    tc::gemm_v_blocks<4><<<bv, threads, 0, s>>>(x, (uint8_t *)Vg, c_in, h, w, tiles_y, tiles_x,
+                                                 (int)T, C16, Tb);
+  else
+    tc::gemm_v_blocks<6><<<bv, threads, 0, s>>>(x, (uint8_t *)Vg, c_in, h, w, tiles_y, tiles_x,
+                                                 (int)T, C16, Tb);
+  cwgk_count_launch();
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cwgk_set_cuda_error((int)e);
+    return -3;
+  }
+  return 0;
+}
+
+int cwgk_gemm_x3(const void *Ug, const void *Vg, float *Mf, int nf, int c_in, int c_out, int T,
+                 void *stream) {
+  const int C16 = (c_in + 15) / 16, Kb = (c_out + 127) / 128, Tb = (T + 127) / 128;
+  if (Kb > 65535 || nf > 65535) return -2;
+  cudaError_t e = smem_attr_once<tc::gemm_freq_x3>(tc::kGemmSmem);
+  if (e == cudaSuccess) {
+    tc::gemm_freq_x3<<<dim3((unsigned)Tb, (unsigned)Kb, (unsigned)nf), tc::kGemmThreads,
+                       tc::kGemmSmem, (cudaStream_t)stream>>>(
+        (const uint8_t *)Ug, (const uint8_t *)Vg, Mf, c_out, T, C16, Kb, Tb);
+    cwgk_count_launch();
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) {
     cwgk_set_cuda_error((int)e);
     return -3;

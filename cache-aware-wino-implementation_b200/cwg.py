@@ -21,9 +21,9 @@ LIB_PATH = os.environ.get("CWG_LIB") or os.path.join(HERE, "lib", "libcwg.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "cwg.h")
 
 # status codes and flags (include/cwg.h)
-OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, ENOMEM, ENODEV = 0, -1, -2, -3, -4, -5, -6
+OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, ENOMEM, ENODEV, ERANGE = 0, -1, -2, -3, -4, -5, -6, -7
 RELU, BF16, FORCE_FFMA, FORCE_TC, TC_SINGLE, TC_FULL16 = 0x1, 0x2, 0x10, 0x20, 0x40, 0x80
-TC_NOPAIR, NO_SPLIT = 0x100, 0x200
+TC_NOPAIR, NO_SPLIT, TC_X3 = 0x100, 0x200, 0x400
 PATH_FFMA, PATH_TC = 1, 2
 ORDER_GRID, ORDER_RUNS, ORDER_ROUND = 0, 1, 2  # cwg_choice.order
 
@@ -222,7 +222,8 @@ def conv3x3_fused_host(x_host: int, U, bias, y_host: int, workspace, workspace_b
 
 
 def device_status(stream=None) -> None:
-    """Raises CwgError(ETIMEOUT) if a bounded device wait gave up since the last check."""
+    """Raises CwgError(ETIMEOUT) if a bounded device wait gave up since the last check, or
+    CwgError(ERANGE) if an fp16 tensor-core operand overflowed."""
     _check(lib().cwg_device_status(_stream(stream)), "device status")
 
 

@@ -45,6 +45,9 @@ extern "C" {
 #define CWG_ETIMEOUT (-4)     /* a bounded device-side wait gave up; results invalid */
 #define CWG_ENOMEM (-5)       /* host or device allocation failed (per-tile entries only) */
 #define CWG_ENODEV (-6)       /* no usable sm_100 device */
+#define CWG_ERANGE (-7)       /* an operand left the range of the kernel's fp16 arithmetic
+                                 (bf16 F(4,3) tensor-core layers: |x| above ~650 or |g|
+                                 above ~900); results invalid, rerun with CWG_TC_X3 */
 
 /* ---- flags for the layer-level calls -------------------------------------- */
 #define CWG_RELU 0x1u        /* fused ReLU after bias */
@@ -59,6 +62,11 @@ extern "C" {
 #define CWG_NO_SPLIT 0x200u  /* bit-reproducible results: never split the C_in reduction of a small
                                 fp32 layer across CTAs (a split adds partial sums atomically, so
                                 the last bits of y vary between runs) */
+#define CWG_TC_X3 0x400u     /* bf16 F(4,3) layers on the tensor cores: three bf16 products per
+                                MAC (hi/lo split of both operands, any bf16 range) instead of the
+                                default two fp16 products (U * V_hi + U * V_lo, ~2/3 of the
+                                time; inputs must stay within fp16's range after the transform,
+                                else cwg_device_status reports CWG_ERANGE) */
 
 /* Kernel paths reported by cwg_select. */
 #define CWG_PATH_FFMA 1 /* warp register-blocked FFMA fused kernel */
@@ -78,8 +86,9 @@ typedef struct cwg_choice {
   long long ctas;    /* CTAs in the grid */
   double gemm_flops; /* 2 * tiles * C_out * C_in * (m+2)^2 */
   double alg_bytes;  /* x + y + U + bias, each touched once */
-  int mma_products;  /* bf16 tensor-core products per multiply-accumulate: 3 (hi/lo split,
-                        fp32-accurate) or 1; 0 on the FFMA path */
+  int mma_products;  /* tensor-core products per multiply-accumulate: 3 (bf16 hi/lo split,
+                        fp32-accurate), 2 (fp16, V split into hi + lo: bf16 F(4,3) layers)
+                        or 1 (bf16); 0 on the FFMA path */
   long long ctas_launched; /* CTAs the launch really uses: `ctas`, or for a layer larger than
                               one wave of CTA pairs, two per co-resident cluster of the current
                               device (B200's 74 TPCs when no device is present) */
@@ -162,9 +171,11 @@ int cwg_conv3x3_fused_host_static(const void *x_host, const void *U, const float
 /* ---- non-fused ablation ---------------------------------------------------- */
 
 /* The same fp32 layer as three passes over HBM, for measuring what the fused
- * kernels save: input transform -> V[(m+2)^2][c_in][T] in `workspace`, one
- * cuBLAS SGEMM per frequency (FP32 math) -> M[(m+2)^2][c_out][T], output
- * transform + bias (+ ReLU with CWG_RELU) -> y; T = n*ceil(h/m)*ceil(w/m).
+ * kernels save: input transform -> V in `workspace`, one GEMM per frequency ->
+ * M[(m+2)^2][c_out][T] fp32, output transform + bias (+ ReLU with CWG_RELU) -> y;
+ * T = n*ceil(h/m)*ceil(w/m).  The GEMM does the arithmetic of the fused kernel
+ * of the same layer: tcgen05 MMAs with the bf16 hi/lo split for m = 2 (V and U
+ * as bf16 UMMA blocks), fp32 FFMA for m = 4 and 6.
  * Mirrors the reference's run_non_fused (src/fused_winograd_kernel.py:116-151),
  * whose math equals run_fused.  U in the CUDA-core layout: produce it with
  * cwg_weight_transform(..., m, CWG_FORCE_FFMA, ...).  m = 2, 4 or 6; fp32 only
@@ -188,9 +199,11 @@ const char *cwg_strerror(int status);
 int cwg_last_cuda_error(void);
 
 /* Synchronises `stream`, then reads and clears the device-side status word
- * that bounded waits inside the kernels set when they give up.  Returns
- * CWG_ETIMEOUT if any kernel since the last call timed out, else CWG_OK (or
- * CWG_ECUDA if the synchronisation itself failed). */
+ * that bounded waits inside the kernels set when they give up, and that the
+ * fp16 tensor-core path sets when an operand leaves fp16's range.  Returns
+ * CWG_ETIMEOUT if any kernel since the last call timed out, else CWG_ERANGE if
+ * an operand overflowed, else CWG_OK (or CWG_ECUDA if the synchronisation
+ * itself failed). */
 int cwg_device_status(void *stream);
 
 /* Self-test of the failure path: launches one CTA whose bounded device wait can

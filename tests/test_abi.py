@@ -181,8 +181,15 @@ def test_selector_64_channel_pair():
 
 def test_selector_launch_plan():
     """Which grid the pair kernel launches (without a device: 74 TPCs, one cluster each)."""
-    small = cwg.select(4, 128, 128, 56, 56)  # 25 tile blocks: one per CTA pair
-    assert small.order == cwg.ORDER_GRID and small.ctas_launched == small.ctas == 50
+    # 26 units (13 tile blocks x 2 channel blocks) below one wave: one unit per CTA pair
+    grid = cwg.select(32, 256, 256, 14, 14)
+    assert grid.order == cwg.ORDER_GRID and grid.ctas_launched == grid.ctas == 52
+    # 25 tile blocks of one channel block below one wave: shorter equal runs on more pairs
+    # (3136 tiles over 74 pairs: 48-tile runs on 66 pairs)
+    small = cwg.select(4, 128, 128, 56, 56)
+    assert small.ctas == 50
+    if not cuda_present():
+        assert small.order == cwg.ORDER_RUNS and small.ctas_launched == 2 * 66
     # config 3: 392 blocks = 5.3 waves -> 73 persistent pairs, each 688 tiles (5 x 128 + 48)
     c3 = cwg.select(64, 128, 128, 56, 56)
     assert c3.ctas == 784
@@ -206,12 +213,15 @@ def test_selector_f43_tensor_core():
     n, c, k, h, w = 2, 128, 200, 30, 30
     tiles = n * 8 * 8  # 4x4 output tiles
     ch = cwg.select(n, c, k, h, w, 4, cwg.BF16)
-    assert ch.path == cwg.PATH_TC and ch.m == 4 and ch.mma_products == 3
+    assert ch.path == cwg.PATH_TC and ch.m == 4 and ch.mma_products == 2
     assert ch.tiles_per_cta == 64 and ch.cout_per_cta == 64
     assert ch.ctas == 2 * (-(-tiles // 64)) * (-(-k // 64))
-    # weights: [ceil(C_out/64)][2 ranks][C_in/16][36 f][hi, lo] blocks of 128 rows
-    # (2 output rows x 64 channels) x 16 channels x bf16
-    assert cwg.weight_bytes(c, k, 4, cwg.BF16) == 4 * 2 * 8 * 36 * 2 * 4096
+    # weights: [ceil(C_out/64)][2 ranks][C_in/16][36 f] fp16 blocks of 128 rows
+    # (2 output rows x 64 channels) x 16 channels; CWG_TC_X3: bf16 hi and lo blocks
+    assert cwg.weight_bytes(c, k, 4, cwg.BF16) == 4 * 2 * 8 * 36 * 4096
+    x3 = cwg.select(n, c, k, h, w, 4, cwg.BF16 | cwg.TC_X3)
+    assert x3.path == cwg.PATH_TC and x3.mma_products == 3
+    assert cwg.weight_bytes(c, k, 4, cwg.BF16 | cwg.TC_X3) == 4 * 2 * 8 * 36 * 2 * 4096
     # bf16 F(2,3) runs single products; fp32 F(2,3) the hi/lo split
     assert cwg.select(n, c, k, h, w, 0, cwg.BF16).mma_products == 1
     assert cwg.select(n, c, k, h, w, 2).mma_products == 3
@@ -227,9 +237,13 @@ def test_selector_f43_tensor_core():
 
 
 def test_nonfused_workspace_and_argument_checks():
-    # V[td^2][C][T] + M[td^2][K][T] fp32, each rounded up to 256 bytes
+    # F(2,3) (tensor-core GEMM): U and V as UMMA blocks of 128 rows x 16 channels, hi and lo
+    # bf16 (8 KiB per block pair), rows padded to 128 and channels to 16; M fp32
     T = 2 * 28 * 28
-    assert cwg.nonfused_workspace_bytes(2, 32, 48, 56, 56, 2) == 16 * 32 * T * 4 + 16 * 48 * T * 4
+    blocks = lambda rows, c: 16 * -(-rows // 128) * -(-c // 16) * 8192  # noqa: E731
+    assert cwg.nonfused_workspace_bytes(2, 32, 48, 56, 56, 2) == \
+        blocks(48, 32) + blocks(T, 32) + 16 * 48 * T * 4
+    # F(4,3), F(6,3) (FFMA GEMM): V[td^2][C][T] + M[td^2][K][T] fp32, each rounded up to 256
     T4 = 1 * 3 * 3
     b = cwg.nonfused_workspace_bytes(1, 5, 7, 9, 10, 4)
     assert b == -(-36 * 5 * T4 * 4 // 256) * 256 + -(-36 * 7 * T4 * 4 // 256) * 256

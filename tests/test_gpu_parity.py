@@ -318,18 +318,48 @@ def test_tensor_core_variants_bf16(cuda_dev, variant):
 F43_TC = [(2, 64, 64, 9, 13), (1, 96, 200, 7, 7), (3, 128, 64, 5, 22), (1, 64, 128, 24, 24)]
 
 
+@pytest.mark.parametrize("products", [0, cwg.TC_X3], ids=["fp16x2", "bf16x3"])
 @pytest.mark.parametrize("case", F43_TC, ids=lambda c: "x".join(map(str, c)))
-def test_tensor_core_f43_bf16(cuda_dev, case):
+def test_tensor_core_f43_bf16(cuda_dev, case, products):
     """F(4,3) on the pair kernel (6 accumulators, two output rows per CTA) for
-    bf16 layers: ragged tiles, partial channel blocks, tile blocks across
-    images."""
+    bf16 layers, in both product modes (fp16 U * (V_hi + V_lo), the default, and
+    the bf16 hi/lo split of CWG_TC_X3): ragged tiles, partial channel blocks,
+    tile blocks across images."""
     n, c, k, h, w = case
     rng = np.random.default_rng(sum(case) + 500)
     x = workloads.bf16_round(rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32))
     g = workloads.bf16_round(rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32))
     bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
-    y = gpu_conv(x, g, bias, 4, cwg.BF16 | cwg.RELU | cwg.FORCE_TC, cuda_dev)
+    y = gpu_conv(x, g, bias, 4, cwg.BF16 | cwg.RELU | cwg.FORCE_TC | products, cuda_dev)
     assert_close(y, oracle.direct_conv_f64(x, g, bias, True), "bf16", f"bf16 {case}")
+
+
+def test_fp16_products_report_range_overflow(cuda_dev):
+    """bf16 data whose Winograd transform leaves fp16's range (|V| up to 100 |x| for
+    F(4,3)) cannot run the fp16 products: the kernel finishes, sets the range bit
+    and cwg_device_status reports CWG_ERANGE; CWG_TC_X3 runs the same layer
+    correctly.  Weights beyond fp16's range are reported by the transform."""
+    import torch
+
+    n, c, k, h, w = 1, 64, 64, 12, 12
+    rng = np.random.default_rng(77)
+    x = workloads.bf16_round(rng.uniform(-2000, 2000, (n, c, h, w)).astype(np.float32))
+    g = workloads.bf16_round(rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32))
+    bias = np.zeros(k, np.float32)
+    flags = cwg.BF16 | cwg.FORCE_TC
+    with pytest.raises(cwg.CwgError) as e:
+        gpu_conv(x, g, bias, 4, flags, cuda_dev)
+    assert e.value.status == cwg.ERANGE
+    cwg.device_status()  # the status word was cleared
+    y = gpu_conv(x, g, bias, 4, flags | cwg.TC_X3, cuda_dev)
+    assert_close(y, oracle.direct_conv_f64(x, g, bias, False), "bf16", "bf16x3, large inputs")
+    # weights: |g| = 1e5 overflows fp16 in the transform itself
+    U = torch.empty(cwg.weight_bytes(c, k, 4, flags), dtype=torch.uint8, device=cuda_dev)
+    g_big = torch.from_numpy(np.full((k, c, 3, 3), 1e5, np.float32)).to(cuda_dev)
+    cwg.weight_transform(g_big, U, c, k, 4, flags)
+    with pytest.raises(cwg.CwgError) as e:
+        cwg.device_status()
+    assert e.value.status == cwg.ERANGE
 
 
 # Layers above one wave of CTA pairs run persistent pairs: each pair walks an
@@ -418,12 +448,15 @@ def test_weight_transform_stays_in_its_buffer(cuda_dev, case):
 
 
 @pytest.mark.parametrize("case", [(2, 32, 48, 15, 17, 2), (1, 128, 128, 56, 56, 2),
+                                  (3, 144, 200, 11, 13, 2), (1, 16, 8, 1, 1, 2),
                                   (1, 64, 64, 21, 19, 4), (2, 16, 32, 9, 9, 4),
-                                  (1, 32, 40, 20, 26, 6)],
+                                  (1, 32, 40, 20, 26, 6), (1, 70, 130, 9, 9, 4)],
                          ids=lambda c: "x".join(map(str, c)))
 def test_nonfused_ablation_matches_reference(cuda_dev, case):
-    """The three-pass ablation (input transform -> HBM -> cuBLAS SGEMM per frequency ->
-    output transform) computes the same layer."""
+    """The three-pass ablation (input transform -> HBM -> per-frequency GEMM: tcgen05 bf16x3
+    for F(2,3), fp32 FFMA for F(4,3)/F(6,3) -> output transform) computes the same layer;
+    ragged tile blocks (T not a multiple of 128), channel counts not multiples of 16 or 128,
+    a one-pixel image."""
     import torch
 
     n, c, k, h, w, m = case
