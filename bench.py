@@ -512,8 +512,8 @@ def bench_layer(layer, args, rk, dev, peaks, peak_src, *, steps: int, warmup: in
             "plan": plan_dict(choice, flags) if not nonfused else
             {"path": "nonfused (input pass, per-frequency GEMM, output pass)", "flags": flags},
             "roofline": roofline(choice, t_max, peaks, peak_src,
-                                 f"cfg{layer.config}.{layer.index}:{choice.path_name}"
-                                 if not nonfused else None),
+                                 f"cfg{layer.config}.{layer.index}:{choice.path_name}")
+            if not nonfused else None,
             "e2e": None if te_ms is None else {
                 "value": flops_total / (te_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": xbytes, "d2h_bytes_per_step": ybytes,

@@ -815,7 +815,13 @@ struct PairGeo {
   static constexpr int kGroups = M == 2 ? 1 : 2;
   static constexpr int kGroupWarps = kXWarps / kGroups;
   static constexpr int kCpt = 2;
-  static constexpr int kNU = HM ? 8 : 5;            // weight stages
+  // weight stages in flight.  Fewer than the stream could use: every KB of
+  // shared memory left unallocated serves as L1 cache for the input windows,
+  // and their misses refill the same SRAM the tensor core reads its operands
+  // from.  Measured on B200 (us/layer, 2 / 3 / 4 / 5 stages): 64 images of
+  // 128->128 at 56x56 (F(2,3), 16 KB stages) 198 / 177 / 179 / 182; 256 images
+  // of 64->64 at 56x56 (8 KB stages, 3 / 4 / 6 / 8) 285 / 286 / 289 / 288.
+  static constexpr int kNU = HM ? 4 : 3;
   static constexpr int kVBytes = kTiles * kCc * 2;  // one frequency of V
   static constexpr int kEpiTiles = 32 / M;          // tiles per 32-pixel epilogue patch row
   static_assert(TD * kN <= kTmemCols, "accumulators fit TMEM");
@@ -879,9 +885,11 @@ template <int M, int PM, bool HM = false>
 struct PairLayout {
   using G = PairGeo<M, HM>;
   using P = Prod<PM>;
-  // weight stages: the one-part fp16 layout keeps the same bytes in flight with
-  // twice the stages
-  static constexpr int kNU = G::kNU * (PM == kPmH2 ? 2 : 1);
+  // weight stages: PairGeo::kNU for F(2,3) (twice that for one-part bf16 stages,
+  // the same bytes in flight); five for F(4,3) (32 images of 256->256 at
+  // 112x112, fp16 stages, 2 / 3 / 4 / 5 / 10 stages: 1959 / 1500 / 1364 / 1356 /
+  // 1368 us)
+  static constexpr int kNU = M == 2 ? G::kNU * (PM == kPmX1 ? 2 : 1) : 5;
   static constexpr int kVStage = P::kVParts * G::NF * G::kVBytes;
   static constexpr int kUStage = kFPerU * P::kUParts * G::kBlkBytes;
   static constexpr int kVOff = 0;
@@ -1486,6 +1494,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       ok = __all_sync(0xffffffffu, mbar_wait(v_empty + 8 * vs, ((s / kNV) & 1) ^ 1, abort));
       if (!ok) break;
       uint8_t *vb = smem + L::kVOff + vs * L::kVStage;
+      const int sn = s + G::kGroups;  // this group's next stage
       if (tb16 < cnt_cta) {
         if constexpr (M == 2) {
           float v[CPT][TD][TD];
@@ -1541,8 +1550,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(v_full + 8 * vs);
+      // the next stage's loads go out after this stage's V stores (issuing them
+      // between the transform and the stores measured 188.8 vs 180.8 us on
+      // 64 images of 128->128 at 56x56)
       if constexpr (M == 2) {
-        const int sn = s + G::kGroups;
         if (sn < S) load_stage(sn);
       }
     }
@@ -1941,43 +1952,59 @@ __global__ void gemm_u_blocks(const float *__restrict__ U, uint8_t *__restrict__
   *reinterpret_cast<__nv_bfloat16 *>(blk + kCoreBytes + off) = lo;
 }
 
-// Input pass of the ablation for the tensor-core GEMM: V = Bt d B of one (channel,
-// tile) written as hi/lo bf16 into the Vg blocks; zero past C and T (the blocks
-// cover the padded ranges, so no memset is needed).
-template <int M>
-__global__ void gemm_v_blocks(const float *__restrict__ x, uint8_t *__restrict__ Vg, int C, int H,
-                              int W, int tiles_y, int tiles_x, int T, int C16, int Tb) {
-  constexpr int TD = M + 2, NF = TD * TD;
+// Input pass of the ablation for the tensor-core GEMM (F(2,3)): V = Bt d B of one
+// tile and 8 input channels, written as hi/lo bf16 into the Vg blocks -- per
+// frequency one 16-byte row of each block, so that consecutive threads (tiles)
+// fill consecutive rows; zero past C and T (the blocks cover the padded ranges,
+// so no memset is needed).
+__global__ void __launch_bounds__(128)
+    gemm_v_blocks(const float *__restrict__ x, uint8_t *__restrict__ Vg, int C, int H, int W,
+                  int tiles_y, int tiles_x, int T, int C16, int Tb) {
+  constexpr int NF = 16;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long Tp = (long long)Tb * 128, Cp = (long long)C16 * 16;
-  if (idx >= Cp * Tp) return;
+  const long long Tp = (long long)Tb * 128;
+  if (idx >= (long long)C16 * 2 * Tp) return;
   const int t = (int)(idx % Tp);
-  const int c = (int)(idx / Tp);
-  float d[TD][TD], v[TD][TD];
-  const bool ok = t < T && c < C;
+  const int c8 = (int)(idx / Tp);  // 8-channel group: channels 8 c8 .. 8 c8 + 7
   const int per_img = tiles_y * tiles_x;
-  const int n = ok ? t / per_img : 0;
-  const int rem = ok ? t - n * per_img : 0;
+  const bool tok = t < T;
+  const int n = tok ? t / per_img : 0;
+  const int rem = tok ? t - n * per_img : 0;
   const int ty = rem / tiles_x, tx = rem - ty * tiles_x;
-  const int y0 = M * ty - 1, x0 = M * tx - 1;
-  const float *xc = x + ((size_t)n * C + (ok ? c : 0)) * H * W;
+  const int y0 = 2 * ty - 1, x0 = 2 * tx - 1;
+  uint32_t hi[NF][4], lo[NF][4];  // per frequency: 8 channels as 4 bf16 pairs
 #pragma unroll
-  for (int i = 0; i < TD; ++i)
+  for (int q2 = 0; q2 < 4; ++q2) {
+    float v[2][4][4];
 #pragma unroll
-    for (int j = 0; j < TD; ++j) {
-      const int yy = y0 + i, xx = x0 + j;
-      d[i][j] = (ok && yy >= 0 && yy < H && xx >= 0 && xx < W) ? xc[(size_t)yy * W + xx] : 0.f;
+    for (int h = 0; h < 2; ++h) {
+      const int c = 8 * c8 + 2 * q2 + h;
+      const bool ok = tok && c < C;
+      const float *xc = x + ((size_t)n * C + (ok ? c : 0)) * H * W;
+      float d[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int yy = y0 + i, xx = x0 + j;
+          d[i][j] =
+              (ok && yy >= 0 && yy < H && xx >= 0 && xx < W) ? xc[(size_t)yy * W + xx] : 0.f;
+        }
+      input_transform<2, true>(d, v[h]);
     }
-  input_transform<M, true>(d, v);
-  const uint32_t off = blk_off(t % 128, c % 16);
+#pragma unroll
+    for (int f = 0; f < NF; ++f)
+      split_pair(v[0][f / 4][f % 4], v[1][f / 4][f % 4], hi[f][q2], lo[f][q2]);
+  }
+  // row t of the block (t / 128, c8 / 2), K half c8 % 2: 8-row groups 256 B apart,
+  // K halves 128 B apart, rows 16 B apart (blk_off)
+  const uint32_t off = blk_off(t % 128, (c8 % 2) * 8);
 #pragma unroll
   for (int f = 0; f < NF; ++f) {
-    const float e = v[f / TD][f % TD];
-    const __nv_bfloat16 hi = __float2bfloat16_rn(e);
-    const __nv_bfloat16 lo = __float2bfloat16_rn(e - __bfloat162float(hi));
-    uint8_t *blk = Vg + ((((size_t)f * Tb + t / 128) * C16 + c / 16) * 2) * kCoreBytes;
-    *reinterpret_cast<__nv_bfloat16 *>(blk + off) = hi;
-    *reinterpret_cast<__nv_bfloat16 *>(blk + kCoreBytes + off) = lo;
+    uint8_t *blk = Vg + ((((size_t)f * Tb + t / 128) * C16 + c8 / 2) * 2) * kCoreBytes;
+    *reinterpret_cast<uint4 *>(blk + off) = make_uint4(hi[f][0], hi[f][1], hi[f][2], hi[f][3]);
+    *reinterpret_cast<uint4 *>(blk + kCoreBytes + off) =
+        make_uint4(lo[f][0], lo[f][1], lo[f][2], lo[f][3]);
   }
 }
 
@@ -2218,6 +2245,7 @@ size_t cwgk_gemm_blocks_bytes(int nf, int rows, int c_in) {
 int cwgk_gemm_prepare(const float *U, void *Ug, const float *x, void *Vg, int m, int n, int c_in,
                       int c_out, int h, int w, void *stream) {
   cudaStream_t s = (cudaStream_t)stream;
+  if (m != 2) return -2;  // the tensor-core ablation serves F(2,3) layers
   const int nf = (m + 2) * (m + 2);
   const int tiles_y = (h + m - 1) / m, tiles_x = (w + m - 1) / m;
   const long long T = (long long)n * tiles_y * tiles_x;
@@ -2228,17 +2256,10 @@ int cwgk_gemm_prepare(const float *U, void *Ug, const float *x, void *Vg, int m,
   tc::gemm_u_blocks<<<(unsigned)((nu + threads - 1) / threads), threads, 0, s>>>(
       U, (uint8_t *)Ug, nf, c_in, c_out, C16, Kb);
   cwgk_count_launch();
-  const long long nv = (long long)C16 * 16 * Tb * 128;
-  const unsigned bv = (unsigned)((nv + threads - 1) / threads);
-  if (m == 2)
-    tc::gemm_v_blocks<2><<<bv, threads, 0, s>>>(x, (uint8_t *)Vg, c_in, h, w, tiles_y, tiles_x,
-                                                 (int)T, C16, Tb);
-  else if (m == 4)
-    tc::gemm_v_blocks<4><<<bv, threads, 0, s>>>(x, (uint8_t *)Vg, c_in, h, w, tiles_y, tiles_x,
-                                                 (int)T, C16, Tb);
-  else
-    tc::gemm_v_blocks<6><<<bv, threads, 0, s>>>(x, (uint8_t *)Vg, c_in, h, w, tiles_y, tiles_x,
-                                                 (int)T, C16, Tb);
+  const long long nv = (long long)C16 * 2 * Tb * 128;
+  const unsigned bv = (unsigned)((nv + 127) / 128);
+  tc::gemm_v_blocks<<<bv, 128, 0, s>>>(x, (uint8_t *)Vg, c_in, h, w, tiles_y, tiles_x, (int)T,
+                                        C16, Tb);
   cwgk_count_launch();
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
