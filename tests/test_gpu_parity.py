@@ -373,6 +373,10 @@ PERSISTENT = [
     (13, 64, 64, 56, 56, 2, cwg.BF16),               # bf16 F(2,3): patches outside the V ring
     (13, 96, 64, 56, 56, 2, 0),                      # fp32 F(2,3), 64 channels: M = 128 pair
     (25, 64, 72, 56, 56, 4, cwg.BF16),               # bf16 F(4,3), 2 ragged channel blocks
+    # below one wave of units: equal runs shorter than an item on more pairs
+    (4, 128, 128, 56, 56, 2, 0),                     # 25 blocks -> 66 runs of 48 tiles
+    (8, 64, 128, 37, 41, 2, 0),                      # odd image sizes: runs across rows
+    (2, 64, 64, 64, 60, 4, cwg.BF16),                # F(4,3): runs of 32-tile items
 ]
 
 
@@ -388,6 +392,7 @@ def test_persistent_pairs(cuda_dev, case):
         x, g = workloads.bf16_round(x), workloads.bf16_round(g)
     ch = cwg.select(n, c, k, h, w, m, cwg.RELU | cwg.FORCE_TC | extra)
     assert ch.path == cwg.PATH_TC
+    assert ch.order in (cwg.ORDER_RUNS, cwg.ORDER_ROUND), ch.order_name
     y = gpu_conv(x, g, bias, m, cwg.RELU | cwg.FORCE_TC | extra, cuda_dev)
     ref = oracle.direct_conv_f64(x, g, bias, True)
     assert_close(y, ref, "bf16" if bf else "f23", f"persistent {case}")
