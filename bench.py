@@ -429,7 +429,6 @@ def bench_layer(layer, args, rk, dev, peaks, peak_src, *, steps: int, warmup: in
         if global_n < world:
             raise SystemExit(f"{global_n} images cannot be split across {world} ranks")
         first, cnt = ranks.shard(global_n, rk)
-    lr = layer.with_n(cnt)
     flags = (cwg.RELU if layer.relu else 0) | (cwg.BF16 if layer.bf16 else 0) | extra_flags
     c, k, h, w, m = layer.c_in, layer.c_out, layer.h, layer.w, layer.m
     nonfused = args.nonfused and layer.config == args.config
@@ -489,7 +488,7 @@ def bench_layer(layer, args, rk, dev, peaks, peak_src, *, steps: int, warmup: in
 
         for _ in range(min(warmup, 3)):
             e2e_step(0)
-        te_ms, e2e_reps, _, _ = timed_loop(e2e_step, max(3, min(steps, 10)),
+        te_ms, _, _, _ = timed_loop(e2e_step, max(3, min(steps, 10)),
                                            args.min_time / 4, rk, dev, stream, False)
         del ws
 
