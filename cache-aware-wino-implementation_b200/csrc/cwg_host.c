@@ -407,7 +407,8 @@ int cwg_conv3x3_fused(const void *x, const void *U, const float *bias, void *y, 
   const int bf16 = (flags & CWG_BF16) ? 1 : 0;
   if (path == CWG_PATH_TC) {
     return cwgk_conv_tc(x, U, bias, y, n, c_in, c_out, h, w, mm, tc_products(mm, flags),
-                        tc_variant(flags, mm, c_out), bf16, relu, !(flags & CWG_NO_SPLIT), stream);
+                        tc_variant(flags, mm, c_out), bf16, relu, !(flags & CWG_NO_SPLIT),
+                        !(flags & CWG_NO_PDL), stream);
   }
   if (small_cin(c_in, mm))
     return cwgk_conv_small(x, U, bias, y, n, c_in, c_out, h, w, bf16, relu, stream);
@@ -509,7 +510,8 @@ int cwgh_conv_host_serial(const void *x_host, const void *U, const float *bias, 
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e = cudaMemcpyAsync(xd, x_host, xbytes, cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return cuda_fail(e);
-  int rc = cwg_conv3x3_fused(xd, U, bias, yd, n, c_in, c_out, h, w, m, flags, s);
+  /* an ordinary launch between the copies: nothing to overlap here */
+  int rc = cwg_conv3x3_fused(xd, U, bias, yd, n, c_in, c_out, h, w, m, flags | CWG_NO_PDL, s);
   if (rc) return rc;
   e = cudaMemcpyAsync(y_host, yd, ybytes, cudaMemcpyDeviceToHost, s);
   if (e != cudaSuccess) return cuda_fail(e);
@@ -604,7 +606,9 @@ int cwg_conv3x3_fused_host(const void *x_host, const void *U, const float *bias,
     if (e == cudaSuccess) e = cudaEventRecord(c->ev_in, c->s_in);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s, c->ev_in, 0);
     if (e != cudaSuccess) return cuda_fail(e);
-    rc = cwg_conv3x3_fused(xd + xo, U, bias, yd + yo, cnt, c_in, c_out, h, w, m, flags, stream);
+    /* ordinary launches: each chunk's kernel follows an event wait on its copy */
+    rc = cwg_conv3x3_fused(xd + xo, U, bias, yd + yo, cnt, c_in, c_out, h, w, m,
+                           flags | CWG_NO_PDL, stream);
     if (rc) return rc;
     e = cudaEventRecord(c->ev_comp, s);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(c->s_out, c->ev_comp, 0);

@@ -87,10 +87,11 @@ int cwgk_bias_relu(float *y, const float *bias, int n, int c_out, int h, int w, 
  * channel block by the weight layout), kernel `variant` (CWGK_TC_*; the
  * single-CTA variants are F(2,3) only).  allow_split: the pair kernel may split
  * the C_in reduction of small fp32 layers across CTAs (y zeroed, partial sums
- * added atomically, bias and ReLU in a second pass). */
+ * added atomically, bias and ReLU in a second pass).  allow_pdl: the pair
+ * kernel is a programmatic dependent launch (see CWG_NO_PDL). */
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
                  int c_out, int h, int w, int m, int pm, int variant, int bf16, int relu,
-                 int allow_split, void *stream);
+                 int allow_split, int allow_pdl, void *stream);
 
 /* C_in slices the tensor-core path uses for this layer (1 = no split). */
 int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant, int bf16,

@@ -707,6 +707,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Programmatic dependent launch: wait for the previous grid of the stream to
+// complete (its memory operations visible); allow the next grid to launch.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile(
       "barrier.cluster.arrive.release.aligned;\n\t"
@@ -1218,6 +1224,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
   }
   __syncthreads();
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
+  // Launched as a programmatic dependent launch, this CTA may have started while
+  // the previous kernel of the stream was still running: nothing above touched
+  // global memory, and nothing below does before that kernel has completed and
+  // its writes are visible.  (Without such a launch both are no-ops.)
+  griddep_wait();
+  griddep_launch_dependents();
 
   if (warp == 0) {
     // ---------------- TMEM (both CTAs) + MMA issue (rank 0) / relay (rank 1) ----------
@@ -1726,7 +1738,7 @@ static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
 template <int M, int PM, typename Tio, bool HM>
 static cudaError_t launch_pair(const void *x, const void *U, const float *bias, void *y, int n,
                                int c, int k, int h, int w, int relu, int allow_split,
-                               cudaStream_t s) {
+                               int allow_pdl, cudaStream_t s) {
   using G = PairGeo<M, HM>;
   using L = PairLayout<M, PM, HM>;
   const int tiles_y = (h + M - 1) / M, tiles_x = (w + M - 1) / M;
@@ -1751,11 +1763,24 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
     return cudaErrorInvalidValue;
   const size_t ybytes = (size_t)n * k * h * w * sizeof(Tio);
   if (splits > 1 && (e = cudaMemsetAsync(y, 0, ybytes, s)) != cudaSuccess) return e;
-  fn<<<dim3((unsigned)(2 * plan.pairs), (unsigned)plan.gy, (unsigned)splits), G::kThreads,
-       L::kSmem, s>>>((const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w, tiles_y,
-                      tiles_x, (int)total, relu, per, splits > 1, (int)plan.chunk,
-                      plan.kb_count);
-  if ((e = cudaGetLastError()) != cudaSuccess || splits == 1) return e;
+  // Programmatic dependent launch: the pair's CTAs may become resident while the
+  // previous kernel in the stream drains (they set up barriers and TMEM, then
+  // wait for its completion before any global access).  After a memset (split
+  // layers) the launch is an ordinary one.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * plan.pairs), (unsigned)plan.gy, (unsigned)splits);
+  cfg.blockDim = dim3((unsigned)G::kThreads);
+  cfg.dynamicSmemBytes = (size_t)L::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (allow_pdl && splits == 1) ? 1 : 0;
+  e = cudaLaunchKernelEx(&cfg, fn, (const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w,
+                         tiles_y, tiles_x, (int)total, relu, per, (int)(splits > 1),
+                         (int)plan.chunk, plan.kb_count);
+  if (e != cudaSuccess || (e = cudaGetLastError()) != cudaSuccess || splits == 1) return e;
   if (relu) e = launch_bias_relu((float *)y, bias, n, k, h, w, relu, sms, s);
   return e;
 }
@@ -2197,7 +2222,7 @@ int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int pm, int va
 
 int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n, int c_in,
                  int c_out, int h, int w, int m, int pm, int variant, int bf16, int relu,
-                 int allow_split, void *stream) {
+                 int allow_split, int allow_pdl, void *stream) {
   using tc::kPmH2;
   using tc::kPmX1;
   using tc::kPmX3;
@@ -2209,13 +2234,13 @@ int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n
         : tc::launch<X3_, HALF_, float>(x, U, bias, y, n, c_in, c_out, h, w, relu, s))
 #define CWG_TC_LAUNCH_PAIR(M_, PM_, HM_)                                                        \
   (bf16 ? tc::launch_pair<M_, PM_, __nv_bfloat16, HM_>(x, U, bias, y, n, c_in, c_out, h, w,   \
-                                                        relu, allow_split, s)                 \
+                                                        relu, allow_split, allow_pdl, s)      \
         : tc::launch_pair<M_, PM_, float, HM_>(x, U, bias, y, n, c_in, c_out, h, w, relu,     \
-                                               allow_split, s))
+                                               allow_split, allow_pdl, s))
   if (pm == kPmH2) {  // bf16 F(4,3) layers only
     if (!(variant == CWGK_TC_PAIR && m == 4 && bf16)) return -2;
     e = tc::launch_pair<4, kPmH2, __nv_bfloat16, false>(x, U, bias, y, n, c_in, c_out, h, w,
-                                                        relu, allow_split, s);
+                                                        relu, allow_split, allow_pdl, s);
   } else if (variant == CWGK_TC_PAIR && m == 2)
     e = x3 ? CWG_TC_LAUNCH_PAIR(2, kPmX3, false) : CWG_TC_LAUNCH_PAIR(2, kPmX1, false);
   else if (variant == CWGK_TC_PAIR64 && m == 2)

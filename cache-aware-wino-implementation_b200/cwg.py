@@ -23,7 +23,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "cwg.h")
 # status codes and flags (include/cwg.h)
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT, ENOMEM, ENODEV, ERANGE = 0, -1, -2, -3, -4, -5, -6, -7
 RELU, BF16, FORCE_FFMA, FORCE_TC, TC_SINGLE, TC_FULL16 = 0x1, 0x2, 0x10, 0x20, 0x40, 0x80
-TC_NOPAIR, NO_SPLIT, TC_X3 = 0x100, 0x200, 0x400
+TC_NOPAIR, NO_SPLIT, TC_X3, NO_PDL = 0x100, 0x200, 0x400, 0x800
 PATH_FFMA, PATH_TC = 1, 2
 ORDER_GRID, ORDER_RUNS, ORDER_ROUND = 0, 1, 2  # cwg_choice.order
 

@@ -67,6 +67,11 @@ extern "C" {
                                 default two fp16 products (U * V_hi + U * V_lo, ~2/3 of the
                                 time; inputs must stay within fp16's range after the transform,
                                 else cwg_device_status reports CWG_ERANGE) */
+#define CWG_NO_PDL 0x800u    /* launch the tensor-core kernel as an ordinary stream launch; by
+                                default it is a programmatic dependent launch: its CTAs may
+                                start (barriers, TMEM) while the previous kernel in the stream
+                                finishes, and wait for that kernel's completion before they
+                                touch global memory */
 
 /* Kernel paths reported by cwg_select. */
 #define CWG_PATH_FFMA 1 /* warp register-blocked FFMA fused kernel */

@@ -631,3 +631,49 @@ def test_errors_and_launch_counter(cuda_dev):
         cwg.conv3x3_fused(x_d, U, None, y_d, 1, 8, 8, 8, 8, 6, cwg.FORCE_TC)
     assert e.value.status == cwg.EUNSUPPORTED
     cwg.device_status()
+
+
+@pytest.mark.parametrize("case", [(4, 128, 128, 28, 28, 2, 0), (2, 128, 128, 30, 34, 4, 0),
+                                  (2, 256, 256, 28, 28, 4, cwg.BF16)],
+                         ids=["f23", "f43", "f43bf16"])
+def test_dependent_launches_ping_pong(cuda_dev, case):
+    """Tensor-core layers launched back to back as programmatic dependent launches, with no
+    host synchronisation: layer i reads buffer i % 2 and writes the other one, so every
+    layer overwrites what the layer before it read.  The chain matches the same chain of
+    ordinary launches bit for bit, and its first layer matches the oracle."""
+    import torch
+
+    n, c, k, h, w, m, extra = case
+    assert c == k
+    rng = np.random.default_rng(sum(case) + 77)
+    bf = bool(extra & cwg.BF16)
+    dt = torch.bfloat16 if bf else torch.float32
+    x = rng.uniform(-1, 1, (n, c, h, w)).astype(np.float32)
+    gs = [rng.normal(0, np.sqrt(2 / (9 * c)), (k, c, 3, 3)).astype(np.float32) for _ in range(6)]
+    bias = rng.uniform(-0.1, 0.1, k).astype(np.float32)
+    if bf:
+        x, gs = workloads.bf16_round(x), [workloads.bf16_round(g) for g in gs]
+    flags = cwg.RELU | cwg.FORCE_TC | cwg.NO_SPLIT | extra
+    Us = [make_U(g, c, k, m, flags, cuda_dev) for g in gs]
+    b_d = _t(bias, cuda_dev)
+    stream = torch.cuda.Stream(cuda_dev)
+    outs = {}
+    for mode in (cwg.NO_PDL, 0):
+        bufs = [_t(x, cuda_dev, dt), torch.full((n, k, h, w), float("nan"), dtype=dt,
+                                                  device=cuda_dev)]
+        first = torch.empty_like(bufs[1])
+        torch.cuda.synchronize(cuda_dev)
+        with torch.cuda.stream(stream):
+            for i, U in enumerate(Us):
+                cwg.conv3x3_fused(bufs[i % 2], U, b_d, bufs[(i + 1) % 2], n, c, k, h, w, m,
+                                  flags | mode, stream)
+                if i == 0:
+                    first.copy_(bufs[1])
+        stream.synchronize()
+        cwg.device_status(stream)
+        outs[mode] = (bufs[len(Us) % 2].float().cpu().numpy(), first.float().cpu().numpy())
+    np.testing.assert_array_equal(outs[0][0], outs[cwg.NO_PDL][0])
+    np.testing.assert_array_equal(outs[0][1], outs[cwg.NO_PDL][1])
+    ref = oracle.direct_conv_f64(x, gs[0], bias, True)
+    assert_close(outs[0][1], ref, "bf16" if bf else ("f23" if m == 2 else "f43"),
+                 f"first layer {case}")
