@@ -80,13 +80,15 @@ static int num_sms(void) {
 /* ---- path decision (depends only on c_in, c_out, m, flags, so that the
  * weight layout chosen at transform time matches the conv call) ----------- */
 /* Tensor-core kernel variant: the 2-SM pair kernel unless a flag asks for one
- * of the single-CTA kernels; F(2,3) layers of at most 64 output channels run
- * the pair kernel with M = 128 (64 channels per CTA), which reads and streams
- * half the weight rows of the M = 256 kernel, whose other half would be zero. */
+ * of the single-CTA kernels.  Layers of at most 64 output channels run it with
+ * 64 channels per CTA: F(2,3) as M = 128 (half the weight rows of the M = 256
+ * kernel, whose other half would be zero), F(4,3) with two output rows x 64
+ * channels per CTA in one pass over all 36 frequencies (the 128-channel form's
+ * two passes would each leave half their rows zero). */
 static int tc_variant(unsigned flags, int m, int c_out) {
   if (flags & CWG_TC_FULL16) return CWGK_TC_FULL16;
   if (flags & CWG_TC_NOPAIR) return CWGK_TC_HALF;
-  return (m == 2 && c_out <= 64) ? CWGK_TC_PAIR64 : CWGK_TC_PAIR;
+  return c_out <= 64 ? CWGK_TC_PAIR64 : CWGK_TC_PAIR;
 }
 
 /* Products per multiply-accumulate on the tensor cores:
@@ -152,6 +154,7 @@ static int layout_of(int path, int m, unsigned flags, int c_out) {
     const int pm = tc_products(m, flags), x3 = pm == 3;
     const int v = tc_variant(flags, m, c_out);
     if (v == CWGK_TC_PAIR && pm == 2) return CWGK_LAYOUT_TC2_H2;
+    if (v == CWGK_TC_PAIR64 && pm == 2) return CWGK_LAYOUT_TC2H_H2;
     if (v == CWGK_TC_PAIR) return x3 ? CWGK_LAYOUT_TC2_X3 : CWGK_LAYOUT_TC2_X1;
     if (v == CWGK_TC_PAIR64) return x3 ? CWGK_LAYOUT_TC2H_X3 : CWGK_LAYOUT_TC2H_X1;
     return x3 ? CWGK_LAYOUT_TC_X3 : CWGK_LAYOUT_TC_X1;
@@ -162,7 +165,7 @@ static int layout_of(int path, int m, unsigned flags, int c_out) {
 }
 
 static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
-  const size_t nf = (size_t)(m + 2) * (m + 2);
+  size_t nf = (size_t)(m + 2) * (m + 2);
   switch (layout) {
     case CWGK_LAYOUT_FFMA_F32: return nf * c_in * c_out * 4;
     case CWGK_LAYOUT_TC_X3:
@@ -171,17 +174,23 @@ static size_t weight_bytes_for(int c_in, int c_out, int m, int layout) {
     case CWGK_LAYOUT_TC2_X1:
     case CWGK_LAYOUT_TC2H_X3:
     case CWGK_LAYOUT_TC2H_X1:
-    case CWGK_LAYOUT_TC2_H2: {
-      /* [ceil(C_out / kb)][sets][C_pad / 16][nf][parts] blocks of `rows` rows x
-       * 16 channels (rows x 32 bytes).  Pair layouts: one set per rank, and a
-       * block's rows are m/2 output rows x kb = rows / (m/2) channels; 128 rows,
-       * or 64 for the 64-channel pair kernel. */
-      const int half = layout == CWGK_LAYOUT_TC2H_X3 || layout == CWGK_LAYOUT_TC2H_X1;
+    case CWGK_LAYOUT_TC2_H2:
+    case CWGK_LAYOUT_TC2H_H2: {
+      /* [ceil(C_out / kb)][passes][sets][C_pad / 16][nf][parts] blocks of `rows`
+       * rows x 16 channels (rows x 32 bytes).  Pair layouts: one set per rank;
+       * 128 channels of one output row per block and m/2 passes (pairs of
+       * output rows; an F(4,3) pass stores the 30 frequencies whose At row pair
+       * is not all zero), or, for layers of at most 64 channels (TC2H), one
+       * pass: 64 channels of one output row (F(2,3)) or of two (F(4,3)). */
+      const int half = layout == CWGK_LAYOUT_TC2H_X3 || layout == CWGK_LAYOUT_TC2H_X1 ||
+                       layout == CWGK_LAYOUT_TC2H_H2;
       const int pair = half || layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1 ||
                        layout == CWGK_LAYOUT_TC2_H2;
-      const size_t rows = half ? 64 : 128;
-      const size_t kb = pair ? rows / (size_t)(m / 2) : 128;
-      const size_t nkb = ((size_t)c_out + kb - 1) / kb;
+      const size_t kb = half ? 64 : 128;
+      const size_t rows = (half && m == 4) ? 128 : kb;
+      const size_t passes = (pair && !half) ? (size_t)(m / 2) : 1;
+      if (pair && !half && m == 4) nf -= (size_t)(m + 2);
+      const size_t nkb = ((size_t)c_out + kb - 1) / kb * passes;
       const size_t c16 = ((size_t)c_in + 15) / 16;
       const size_t parts = (layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3 ||
                             layout == CWGK_LAYOUT_TC2H_X3)

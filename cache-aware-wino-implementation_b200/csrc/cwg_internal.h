@@ -21,7 +21,8 @@ enum {
   CWGK_LAYOUT_TC2_X1 = 6,    /* pair kernel: At-scaled blocks, single product     */
   CWGK_LAYOUT_TC2H_X3 = 7,   /* 64-channel pair kernel: 64-row hi+lo blocks       */
   CWGK_LAYOUT_TC2H_X1 = 8,   /* 64-channel pair kernel: 64-row blocks, 1 product  */
-  CWGK_LAYOUT_TC2_H2 = 9     /* pair kernel: At-scaled fp16 blocks (F(4,3), bf16) */
+  CWGK_LAYOUT_TC2_H2 = 9,    /* pair kernel: At-scaled fp16 blocks (F(4,3), bf16) */
+  CWGK_LAYOUT_TC2H_H2 = 10   /* the same for F(4,3) layers of <= 64 channels      */
 };
 
 /* Tensor-core kernel variants. */
@@ -29,7 +30,8 @@ enum {
   CWGK_TC_PAIR = 0,   /* 2-SM pair, M = 256 (stacked output rows), F(2,3) and F(4,3) */
   CWGK_TC_HALF = 1,   /* one CTA, half-folded, M = 128, N = 64                  */
   CWGK_TC_FULL16 = 2, /* one CTA, 16 frequency accumulators, N = 32             */
-  CWGK_TC_PAIR64 = 3  /* 2-SM pair, M = 128: 64 output channels, F(2,3) only     */
+  CWGK_TC_PAIR64 = 3  /* 2-SM pair, 64 output channels per CTA: F(2,3) M = 128;
+                         F(4,3) two output rows x 64 channels                   */
 };
 
 /* One compiled FFMA kernel configuration. */

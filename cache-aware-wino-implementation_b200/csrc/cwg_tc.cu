@@ -674,15 +674,17 @@ static cudaError_t launch(const void *x, const void *U, const float *bias, void 
 // A CTA pair (a cluster of two, on the two SMs of one TPC) computes one block
 // of output channels x N tiles.  The half-folded accumulation
 // Z[i][b] = sum_a At[i][a] M[a][b] is stacked along M = 256:
-//   A = [At[0][a] U_ab ; ... ; At[m-1][a] U_ab]  -- the rows of every output-row
-//        index i, pre-scaled by At (exact in bf16); rank r holds 128 of them;
-//   B = V_ab of the pair's N tiles               -- rank r holds half of them;
+//   A = [At[i0][a] U_ab ; At[i0 + 1][a] U_ab]  -- the rows of two output-row
+//        indices, pre-scaled by At (exact in bf16); rank r holds those of
+//        i0 + r (128 output channels);
+//   B = V_ab of the pair's N tiles             -- rank r holds half of them;
 //   D = Z[i][b]: rank r's TMEM holds, for its rows, (m+2) accumulators x N.
-// F(2,3): 128 channels x 128 tiles, rank r = output row 2ty + r.  F(4,3): 64
-// channels x 64 tiles, rank r = output rows 4ty + 2r, 4ty + 2r + 1.  One MMA
-// per (frequency, product) serves every output row and N tiles: for F(2,3) the
-// tensor core reads 6 KB of shared memory per 262K MACs of an SM instead of
-// 6 KB per 131K in the single-CTA kernel.
+// F(2,3): 128 channels x 128 tiles, rank r = output row 2ty + r.  F(4,3): 128
+// channels x 64 tiles per pass, pass p: rank r = output row 4ty + 2p + r; a
+// pass multiplies only the 30 frequencies whose two At rows are not both zero.
+// One MMA per (frequency, product) serves both output rows and N tiles: for
+// F(2,3) the tensor core reads 6 KB of shared memory per 262K MACs of an SM
+// instead of 6 KB per 131K in the single-CTA kernel.
 //
 // Rank 0 issues every MMA and commit for the pair.  Readiness of rank 1's
 // operands reaches rank 0 by remote mbarrier arrivals: rank 1's warp 0 (idle
@@ -792,20 +794,35 @@ constexpr unsigned kStatusRange = 2u;
 // Geometry of the pair kernel for F(M x M, 3x3).
 //   F(2,3): rank r holds the 128 rows (i = r, output channel), 64 tiles of V;
 //           N = 128, 4 accumulators Z[r][b] x 128 columns.
-//   F(4,3): rank r holds 2 x 64 rows (i = 2r + il, output channel), 32 tiles
-//           of V; N = 64, 6 accumulators x 64 columns.
+//   F(4,3): two passes (items) per channel block; in pass p rank r holds the
+//           128 rows of output row i = 2p + r (output channel), 32 tiles of V;
+//           N = 64, 6 accumulators x 64 columns.  (Two rows x 64 channels per
+//           rank and all 36 frequencies, the earlier form: 1346 vs 1272 us on
+//           32 images of 256->256 at 112x112.)
 //   HM ("half M", F(2,3) layers of at most 64 output channels): M = 128, rank r
 //           holds 64 rows (i = r, output channel); in TMEM the accumulator's
 //           columns [0, N/2) sit in lanes 0-63 and [N/2, N) in lanes 64-127,
 //           both at columns 0 .. N/2-1.
-template <int M, bool HM = false>
+template <int M, bool HM = false, int RP = 1>
 struct PairGeo {
   static_assert(!HM || M == 2, "the M = 128 pair kernel is F(2,3) only");
+  static_assert(RP == 1 || (M == 4 && !HM && RP == 2), "two rows per CTA: F(4,3) only");
   static constexpr int TD = M + 2, NF = TD * TD;
-  static constexpr int kRowsI = M / 2;              // output rows i per CTA
+  // A pass of the pair computes RP output rows of every tile on each rank
+  // (rank r: rows (2p + r) RP ..), for kCoutCta output channels.  F(4,3) with
+  // RP = 1 runs two passes (rows 0-1, rows 2-3) as separate items; each skips
+  // the frequency row a that both of its At rows leave zero (a = 5 for rows 0
+  // and 1, a = 0 for rows 2 and 3), so a pass multiplies 30 of the 36
+  // frequencies.  RP = 2 (layers of at most 64 output channels): one pass, 2
+  // rows x 64 channels per rank, all 36 frequencies.
+  static constexpr int kPasses = M / 2 / RP;
+  static constexpr int kRowsI = RP;                 // output rows i per CTA and pass
   static constexpr int kRowsCta = HM ? 64 : kCout;  // A rows (MMA M / 2) per CTA
   static constexpr int kMmaM = 2 * kRowsCta;        // MMA M of the pair
-  static constexpr int kCoutCta = kRowsCta / kRowsI;  // output channels per CTA
+  static constexpr int kCoutCta = kRowsCta / RP;    // output channels per CTA
+  static constexpr int NFP = (M == 4 && RP == 1) ? NF - TD : NF;  // frequencies a pass multiplies
+  // first frequency of pass p (frequencies f0 .. f0 + NFP - 1, f = a * TD + b)
+  __host__ __device__ static constexpr int f0(int p) { return (M == 4 && RP == 1 && p) ? TD : 0; }
   static constexpr int kBlkBytes = kRowsCta * kCc * 2;  // one weight block (rows x 16 ch)
   static constexpr int kTiles = M == 2 ? 64 : 32;   // V columns (tiles) per CTA
   static constexpr int kN = 2 * kTiles;             // MMA N of the pair
@@ -834,17 +851,17 @@ struct PairGeo {
   static_assert(kTiles * kCc == kGroupWarps * 32 * kCpt, "one (tile, channels) per thread");
 };
 
-// Pair weight layout: [ceil(C_out/cout_cta)][rank = 2][C_pad/16][NF f][parts][block]
-// (blocks of rows_cta rows x 16 channels: 4096 B, or 2048 B for HM):
-// block row il * cout_cta + k' of rank r holds At[r * rows_i + il][a] * U_ab for
-// output channel kblk * cout_cta + k' (scaling by 0, +-1, +-2, +-4, +-8 is exact
-// in bf16 and fp16).  Channels past C_out / C_in are zero.  Parts: bf16 hi and
+// Pair weight layout: [ceil(C_out/cout_cta)][pass][rank = 2][C_pad/16][NFP f][parts][block]
+// (blocks of rows_cta rows x 16 channels: 4096 B, or 2048 B for HM; a pass
+// stores its NFP frequencies f0(pass) ..): block row k' of rank r holds
+// At[2 pass + r][a] * U_ab for output channel kblk * cout_cta + k' (scaling by
+// 0, +-1, +-2, +-4, +-8 is exact in bf16 and fp16).  Channels past C_out / C_in are zero.  Parts: bf16 hi and
 // lo (kPmX3), one bf16 block (kPmX1) or one fp16 block (kPmH2).  An fp16 weight
 // beyond the fp16 range sets the range bit of the status word.
-template <int M, int PM, bool HM>
+template <int M, int PM, bool HM, int RP = 1>
 __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__restrict__ U,
                                      int C, int K, int Cp, int Kp, int from_ref) {
-  using G = PairGeo<M, HM>;
+  using G = PairGeo<M, HM, RP>;
   using P = Prod<PM>;
   constexpr int NF = G::NF, TD = G::TD;
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -862,15 +879,18 @@ __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__r
   const int kb = k / G::kCoutCta, kr = k % G::kCoutCta;
   float umax = 0.f;
 #pragma unroll
-  for (int r = 0; r < 2; ++r)
+  for (int pass = 0; pass < G::kPasses; ++pass)
 #pragma unroll
-    for (int il = 0; il < G::kRowsI; ++il) {
-      const long blk0 = ((long)kb * 2 + r) * C16 + c / kCc;
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int il = 0; il < G::kRowsI; ++il) {
+      const long blk0 = (((long)kb * G::kPasses + pass) * 2 + r) * C16 + c / kCc;
       const uint32_t off = blk_off(il * G::kCoutCta + kr, c % kCc);
 #pragma unroll
-      for (int f = 0; f < NF; ++f) {
-        const float s = Wino<M>::at(r * G::kRowsI + il, f / TD) * u[f];
-        uint8_t *b = U + ((blk0 * NF + f) * parts) * G::kBlkBytes;
+      for (int fp = 0; fp < G::NFP; ++fp) {
+        const int f = G::f0(pass) + fp;
+        const float s = Wino<M>::at((2 * pass + r) * G::kRowsI + il, f / TD) * u[f];
+        uint8_t *b = U + ((blk0 * G::NFP + fp) * parts) * G::kBlkBytes;
         if constexpr (P::kF16) {
           *reinterpret_cast<__half *>(b + off) = __float2half_rn(s);
           umax = fmaxf(umax, fabsf(s));
@@ -887,9 +907,9 @@ __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__r
 }
 
 // Shared memory of one CTA of the pair.
-template <int M, int PM, bool HM = false>
+template <int M, int PM, bool HM = false, int RP = 1>
 struct PairLayout {
-  using G = PairGeo<M, HM>;
+  using G = PairGeo<M, HM, RP>;
   using P = Prod<PM>;
   // weight stages: PairGeo::kNU for F(2,3) (twice that for one-part bf16 stages,
   // the same bytes in flight); five for F(4,3) (32 images of 256->256 at
@@ -920,7 +940,7 @@ struct PairLayout {
   static constexpr int kPatchOff = (kAbortSlot + 4 + 127) / 128 * 128;
   static constexpr int kSmem = kPatchInV ? kAbortSlot + 4 : kPatchOff + kPatchBytes;
   static_assert(kSmem <= 227 * 1024, "fits the opt-in shared memory of one CTA");
-  static_assert(G::NF % kFPerU == 0, "whole frequencies per weight stage");
+  static_assert(G::NFP % kFPerU == 0, "whole frequencies per weight stage");
 };
 
 // Work of one CTA pair p = blockIdx.x / 2, as a sequence of items.
@@ -979,14 +999,14 @@ constexpr int kBarEpi = 2;
 // every item's epilogue, also after an abort (then only its barrier arrivals), so
 // that the named barriers match.  Not inlined: its registers stay out of the
 // transform loop, which calls it once per item.
-template <int M, int PM, typename Tio, bool HM>
+template <int M, int PM, typename Tio, bool HM, int RP>
 __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *smem,
                                            const float *__restrict__ bias, Tio *__restrict__ y,
                                            int K, int H, int W, int tiles_y, int tiles_x,
                                            int total_tiles, int chunk, int kb_count,
                                            int relu, int split) {
-  using L = PairLayout<M, PM, HM>;
-  using G = PairGeo<M, HM>;
+  using L = PairLayout<M, PM, HM, RP>;
+  using G = PairGeo<M, HM, RP>;
   constexpr int TD = G::TD, kN = G::kN, kNU = L::kNU;
   constexpr int kEpiThreads = 32 * G::kXWarps;
   const uint32_t sbase = smem_u32(smem);
@@ -1007,7 +1027,8 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
   const int quad = warp & 3;
   // TMEM lanes 32 quad .. 32 quad + 31: channels kq .. kq + 31 of output row
   // irow; HM: lanes 64-127 repeat channels 0-63 for the second half of the columns
-  const int kq = it.kb * G::kCoutCta + (HM ? 32 * (quad & 1) : (quad * 32) % G::kCoutCta);
+  const int kq = (it.kb / G::kPasses) * G::kCoutCta +
+                 (HM ? 32 * (quad & 1) : (quad * 32) % G::kCoutCta);
   // a split adds its partial sums into y (zeroed by the host); slice 0 adds
   // the bias unless a ReLU must follow the full sum, in which case a separate
   // pass applies both once every slice has landed
@@ -1019,7 +1040,8 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
     constexpr int kE = G::kEpiTiles;
     const uint32_t tmem = *tmem_slot;
     const int il = HM ? 0 : (quad * 32) / G::kCoutCta;
-    const int irow = (int)rank * G::kRowsI + il;  // output row i of the tile
+    // output row i of the tile
+    const int irow = (2 * (it.kb % G::kPasses) + (int)rank) * G::kRowsI + il;
     // item columns [col0, lim) of this warp, at TMEM column (column - tshift):
     // 32 (F2) or 16 (F4) per warp; HM: 16 per warp within its lanes' half
     int col0 = (tw >> 2) * (kN / 4), lim = it.cnt, tshift = 0;
@@ -1162,19 +1184,19 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
   return run;
 }
 
-template <int M, int PM, typename Tio, bool HM>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThreads, 1)
+template <int M, int PM, typename Tio, bool HM, int RP = 1>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM, RP>::kThreads, 1)
     wino_fused_tc_pair(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                        const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
                        int W, int tiles_y, int tiles_x, int total_tiles, int relu,
                        int cs_per_split, int split, int chunk, int kb_count) {
-  using L = PairLayout<M, PM, HM>;
-  using G = PairGeo<M, HM>;
+  using L = PairLayout<M, PM, HM, RP>;
+  using G = PairGeo<M, HM, RP>;
   constexpr int UP = L::P::kUParts, TD = G::TD, NF = G::NF;
   constexpr int kTiles = G::kTiles, kN = G::kN, kNU = L::kNU, kVBytes = G::kVBytes;
   constexpr int kXW = G::kXWarps;
   constexpr int kEpiThreads = 32 * kXW;
-  constexpr int kUPerStage = NF / kFPerU;  // weight stages per 16-channel stage
+  constexpr int kUPerStage = G::NFP / kFPerU;  // weight stages per 16-channel stage (a pass)
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = smem_u32(smem);
   const uint32_t v_full = sbase + L::kBarOff, v_empty = v_full + 8 * kNV;
@@ -1251,6 +1273,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       for (int j = 0; ok && j < n_items; ++j) {
         const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
         const uint32_t idesc = instr_desc(G::kMmaM, item_n(it.cnt), L::P::kF16);
+        const int fb = G::f0(it.kb % G::kPasses);  // the pass's first frequency
         if (j > 0) {
           // both CTAs' epilogue warps have read item j-1's accumulators
           ok = __all_sync(0xffffffffu, mbar_wait(tmem_empty, (j - 1) & 1, abort));
@@ -1275,12 +1298,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
             const uint64_t ast = a0 + (uint64_t)((uint32_t)(us * L::kUStage) >> 4);
 #pragma unroll
             for (int fi = 0; fi < kFPerU; ++fi) {
-              const int f = fp * kFPerU + fi;
+              const int f = fb + fp * kFPerU + fi;
               const uint64_t ah = ast + (uint64_t)((uint32_t)(fi * UP * G::kBlkBytes) >> 4);
               const uint64_t bh = bst + (uint64_t)((uint32_t)(f * kVBytes) >> 4);
-              // accumulator Z[.][b], b = f % TD; its first term is a = 0 of stage 0
+              // accumulator Z[.][b], b = f % TD; its first term is the pass's
+              // first row a of stage 0
               const uint32_t d = tmem + (uint32_t)((f % TD) * kN);
-              const uint32_t first = (cs > 0 || f >= TD) ? 1u : 0u;
+              const uint32_t first = (cs > 0 || f >= fb + TD) ? 1u : 0u;
               if (elect_one()) mma_pair_bf16(d, ah, bh, idesc, first);
               if (PM != kPmX1) {  // U * V_lo
                 if (elect_one()) mma_pair_bf16(d, ah, bh + kLo, idesc, 1u);
@@ -1339,7 +1363,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
     bool ok = true;
     for (int j = 0; ok && j < n_items; ++j) {
       const PairItem it = pair_item<kN>(chunk, total_tiles, kb_count, j);
-      const uint8_t *ublk = U + ((size_t)it.kb * 2 + rank) * C16 * NF * UP * G::kBlkBytes +
+      const uint8_t *ublk = U + ((size_t)it.kb * 2 + rank) * C16 * G::NFP * UP * G::kBlkBytes +
                             (size_t)cs0 * kUPerStage * L::kUStage;
       for (int q = 0; q < nst * kUPerStage; ++q) {
         const int s = issued % kNU;
@@ -1497,7 +1521,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       // (F(2,3): stage s's patches are already in registers, their loads having
       // overlapped the last MMAs and the epilogue)
       while (ep < n_items && s > (ep + 1) * nst)
-        ok = pair_epilogue<M, PM, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
+        ok = pair_epilogue<M, PM, Tio, HM, RP>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
                                            tiles_x, total_tiles, chunk, kb_count, relu, split) &&
              ok;
       if (!ok) break;
@@ -1570,7 +1594,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM>::kThr
       }
     }
     while (ep < n_items)
-      ok = pair_epilogue<M, PM, Tio, HM>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
+      ok = pair_epilogue<M, PM, Tio, HM, RP>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
                                          total_tiles, chunk, kb_count, relu, split) &&
            ok;
     if (n_items == 0) named_bar_sync(kBarTmem, 32 + kEpiThreads);
@@ -1648,12 +1672,13 @@ static cudaError_t launch_bias_relu(float *y, const float *bias, int n, int k, i
 // split.  (Above that occupancy the extra zeroing, atomics and bias pass cost
 // more than the shorter C_in loop saves.  One-stage slices rather than two:
 // resnet18's 13 stride-1 layers at N=1, one CUDA graph, 248.7 -> 226.0 us.)
-template <int M, bool HM>
+template <int M, bool HM, int RP = 1>
 static int split_stages(int n, int c, int k, int h, int w, int tpcs, int *per) {
-  using G = PairGeo<M, HM>;
+  using G = PairGeo<M, HM, RP>;
   const int C16 = (c + kCc - 1) / kCc;
   const long long tiles = (long long)n * ((h + M - 1) / M) * ((w + M - 1) / M);
-  const long long items = (tiles + G::kN - 1) / G::kN * ((k + G::kCoutCta - 1) / G::kCoutCta);
+  const long long items =
+      (tiles + G::kN - 1) / G::kN * ((k + G::kCoutCta - 1) / G::kCoutCta) * G::kPasses;
   *per = C16;
   if (4 * items > tpcs || C16 < 2) return 1;
   long long s = tpcs / items;
@@ -1735,28 +1760,28 @@ static PairPlan plan_pairs(long long total, int gy, int splits, int resident) {
   return p;
 }
 
-template <int M, int PM, typename Tio, bool HM>
+template <int M, int PM, typename Tio, bool HM, int RP = 1>
 static cudaError_t launch_pair(const void *x, const void *U, const float *bias, void *y, int n,
                                int c, int k, int h, int w, int relu, int allow_split,
                                int allow_pdl, cudaStream_t s) {
-  using G = PairGeo<M, HM>;
-  using L = PairLayout<M, PM, HM>;
+  using G = PairGeo<M, HM, RP>;
+  using L = PairLayout<M, PM, HM, RP>;
   const int tiles_y = (h + M - 1) / M, tiles_x = (w + M - 1) / M;
   const long long total = (long long)n * tiles_y * tiles_x;
-  const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
+  const int gy = (k + G::kCoutCta - 1) / G::kCoutCta * G::kPasses;  // (channel block, pass)
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   int per = (c + kCc - 1) / kCc;
-  const int splits = (allow_split && sizeof(Tio) == 4) ? split_stages<M, HM>(n, c, k, h, w, sms / 2,
+  const int splits = (allow_split && sizeof(Tio) == 4) ? split_stages<M, HM, RP>(n, c, k, h, w, sms / 2,
                                                                          &per)
                                                        : 1;
-  auto fn = wino_fused_tc_pair<M, PM, Tio, HM>;
-  e = smem_attr_once<wino_fused_tc_pair<M, PM, Tio, HM>>(L::kSmem);
+  auto fn = wino_fused_tc_pair<M, PM, Tio, HM, RP>;
+  e = smem_attr_once<wino_fused_tc_pair<M, PM, Tio, HM, RP>>(L::kSmem);
   if (e != cudaSuccess) return e;
   const int resident =
-      resident_pairs<wino_fused_tc_pair<M, PM, Tio, HM>>(G::kThreads, L::kSmem, sms);
+      resident_pairs<wino_fused_tc_pair<M, PM, Tio, HM, RP>>(G::kThreads, L::kSmem, sms);
   const PairPlan plan = plan_pairs<M, HM>(total, gy, splits, resident);
   // tile indices, item counts and units are 32-bit in the kernel
   if (total * gy > 0x7fffffffLL || 2 * plan.pairs > 0x7fffffffLL || plan.gy > 65535)
@@ -1787,20 +1812,20 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
 
 // The launch plan of a layer as launch_pair would make it on the current device
 // (without one: `sms` SMs and one cluster per TPC).
-template <int M, int PM, typename Tio, bool HM>
+template <int M, int PM, typename Tio, bool HM, int RP = 1>
 static void plan_layer(int n, int c, int k, int h, int w, int allow_split, int sms,
                        long long *ctas, int *order) {
-  using G = PairGeo<M, HM>;
-  using L = PairLayout<M, PM, HM>;
+  using G = PairGeo<M, HM, RP>;
+  using L = PairLayout<M, PM, HM, RP>;
   const long long total = (long long)n * ((h + M - 1) / M) * ((w + M - 1) / M);
-  const int gy = (k + G::kCoutCta - 1) / G::kCoutCta;
+  const int gy = (k + G::kCoutCta - 1) / G::kCoutCta * G::kPasses;  // (channel block, pass)
   int per = 0;
   const int splits =
-      (allow_split && sizeof(Tio) == 4) ? split_stages<M, HM>(n, c, k, h, w, sms / 2, &per) : 1;
+      (allow_split && sizeof(Tio) == 4) ? split_stages<M, HM, RP>(n, c, k, h, w, sms / 2, &per) : 1;
   int resident = sms / 2, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess &&
-      smem_attr_once<wino_fused_tc_pair<M, PM, Tio, HM>>(L::kSmem) == cudaSuccess)
-    resident = resident_pairs<wino_fused_tc_pair<M, PM, Tio, HM>>(G::kThreads, L::kSmem, sms);
+      smem_attr_once<wino_fused_tc_pair<M, PM, Tio, HM, RP>>(L::kSmem) == cudaSuccess)
+    resident = resident_pairs<wino_fused_tc_pair<M, PM, Tio, HM, RP>>(G::kThreads, L::kSmem, sms);
   else
     (void)cudaGetLastError();
   const PairPlan p = plan_pairs<M, HM>(total, gy, splits, resident);
@@ -2080,7 +2105,19 @@ int cwgk_tc_get_cfg(int pm, int variant, int m, cwgk_tc_cfg *out) {
     } else {
       return -1;
     }
-    out->ctas_per_tile_block = 2;
+    // a CTA pair per (tile block, channel block, pass of output rows)
+    out->ctas_per_tile_block = 2 * (m == 4 ? PairGeo<4>::kPasses : PairGeo<2>::kPasses);
+    return 0;
+  }
+  if (variant == CWGK_TC_PAIR64 && m == 4) {  // two output rows x 64 channels per CTA
+    using G4 = PairGeo<4, false, 2>;
+    out->tiles = G4::kN;
+    out->kb = G4::kCoutCta;
+    out->threads = G4::kThreads;
+    out->smem = pm == kPmX3 ? PairLayout<4, kPmX3, false, 2>::kSmem
+                            : (pm == kPmH2 ? PairLayout<4, kPmH2, false, 2>::kSmem
+                                           : PairLayout<4, kPmX1, false, 2>::kSmem);
+    out->ctas_per_tile_block = 2 * G4::kPasses;
     return 0;
   }
   if (pm == kPmH2) return -1;
@@ -2113,15 +2150,18 @@ int cwgk_tc_get_cfg(int pm, int variant, int m, cwgk_tc_cfg *out) {
 
 int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int m, int layout,
                              int from_ref, void *stream) {
-  const bool half = layout == CWGK_LAYOUT_TC2H_X3 || layout == CWGK_LAYOUT_TC2H_X1;
-  const bool h2 = layout == CWGK_LAYOUT_TC2_H2;
+  // TC2H: 64 output channels per CTA (F(2,3): M = 128 pair; F(4,3): two rows x 64)
+  const bool half = layout == CWGK_LAYOUT_TC2H_X3 || layout == CWGK_LAYOUT_TC2H_X1 ||
+                    layout == CWGK_LAYOUT_TC2H_H2;
+  const bool h2 = layout == CWGK_LAYOUT_TC2_H2 || layout == CWGK_LAYOUT_TC2H_H2;
   const bool pair = half || h2 || layout == CWGK_LAYOUT_TC2_X3 || layout == CWGK_LAYOUT_TC2_X1;
   const bool x3 = layout == CWGK_LAYOUT_TC_X3 || layout == CWGK_LAYOUT_TC2_X3 ||
                   layout == CWGK_LAYOUT_TC2H_X3;
-  if (!(m == 2 || (m == 4 && pair && !half))) return -2;
+  if (!(m == 2 || (m == 4 && pair))) return -2;
   if (h2 && m != 4) return -2;
   if (!pair && layout != CWGK_LAYOUT_TC_X1 && layout != CWGK_LAYOUT_TC_X3) return -2;
-  const int kb = half ? tc::PairGeo<2, true>::kCoutCta
+  const int kb = half ? (m == 4 ? tc::PairGeo<4, false, 2>::kCoutCta
+                                : tc::PairGeo<2, true>::kCoutCta)
                       : (pair ? (m == 2 ? tc::PairGeo<2>::kCoutCta : tc::PairGeo<4>::kCoutCta)
                               : tc::kCout);
   const int Cp = (c_in + tc::kCc - 1) / tc::kCc * tc::kCc;
@@ -2137,6 +2177,13 @@ int cwgk_weight_transform_tc(const float *src, void *U, int c_in, int c_out, int
       CWG_WT(tc::wt_transform_tc<true>);
     else
       CWG_WT(tc::wt_transform_tc<false>);
+  } else if (half && m == 4) {
+    if (x3)
+      CWG_WT((tc::wt_transform_tc_pair<4, tc::kPmX3, false, 2>));
+    else if (h2)
+      CWG_WT((tc::wt_transform_tc_pair<4, tc::kPmH2, false, 2>));
+    else
+      CWG_WT((tc::wt_transform_tc_pair<4, tc::kPmX1, false, 2>));
   } else if (half) {
     if (x3)
       CWG_WT((tc::wt_transform_tc_pair<2, tc::kPmX3, true>));
@@ -2192,13 +2239,24 @@ int cwgk_tc_splits(int n, int c_in, int c_out, int h, int w, int m, int variant,
 int cwgk_tc_plan(int n, int c_in, int c_out, int h, int w, int m, int pm, int variant, int bf16,
                  int allow_split, int sms, long long *ctas, int *order) {
   using namespace tc;
-  if (!(variant == CWGK_TC_PAIR && (m == 2 || m == 4)) && !(variant == CWGK_TC_PAIR64 && m == 2))
+  if (!((variant == CWGK_TC_PAIR || variant == CWGK_TC_PAIR64) && (m == 2 || m == 4)))
     return -1;
   if (pm == kPmH2 && !(m == 4 && bf16)) return -1;
 #define CWG_PLAN(M_, PM_, T_, HM_) \
   plan_layer<M_, PM_, T_, HM_>(n, c_in, c_out, h, w, allow_split, sms, ctas, order)
   const bool x3 = pm == kPmX3;
-  if (variant == CWGK_TC_PAIR64) {
+  if (variant == CWGK_TC_PAIR64 && m == 4) {  // bf16 layers only
+    if (!bf16) return -1;
+    if (pm == kPmH2)
+      plan_layer<4, kPmH2, __nv_bfloat16, false, 2>(n, c_in, c_out, h, w, allow_split, sms,
+                                                     ctas, order);
+    else if (x3)
+      plan_layer<4, kPmX3, __nv_bfloat16, false, 2>(n, c_in, c_out, h, w, allow_split, sms,
+                                                     ctas, order);
+    else
+      plan_layer<4, kPmX1, __nv_bfloat16, false, 2>(n, c_in, c_out, h, w, allow_split, sms,
+                                                     ctas, order);
+  } else if (variant == CWGK_TC_PAIR64) {
     if (bf16)
       x3 ? CWG_PLAN(2, kPmX3, __nv_bfloat16, true) : CWG_PLAN(2, kPmX1, __nv_bfloat16, true);
     else
@@ -2237,7 +2295,18 @@ int cwgk_conv_tc(const void *x, const void *U, const float *bias, void *y, int n
                                                         relu, allow_split, allow_pdl, s)      \
         : tc::launch_pair<M_, PM_, float, HM_>(x, U, bias, y, n, c_in, c_out, h, w, relu,     \
                                                allow_split, allow_pdl, s))
-  if (pm == kPmH2) {  // bf16 F(4,3) layers only
+  if (variant == CWGK_TC_PAIR64 && m == 4) {  // bf16 F(4,3), two rows x 64 channels per CTA
+    if (!bf16) return -2;
+    if (pm == kPmH2)
+      e = tc::launch_pair<4, kPmH2, __nv_bfloat16, false, 2>(x, U, bias, y, n, c_in, c_out, h, w,
+                                                             relu, allow_split, allow_pdl, s);
+    else if (x3)
+      e = tc::launch_pair<4, kPmX3, __nv_bfloat16, false, 2>(x, U, bias, y, n, c_in, c_out, h, w,
+                                                             relu, allow_split, allow_pdl, s);
+    else
+      e = tc::launch_pair<4, kPmX1, __nv_bfloat16, false, 2>(x, U, bias, y, n, c_in, c_out, h, w,
+                                                             relu, allow_split, allow_pdl, s);
+  } else if (pm == kPmH2) {  // bf16 F(4,3) layers only
     if (!(variant == CWGK_TC_PAIR && m == 4 && bf16)) return -2;
     e = tc::launch_pair<4, kPmH2, __nv_bfloat16, false>(x, U, bias, y, n, c_in, c_out, h, w,
                                                         relu, allow_split, allow_pdl, s);

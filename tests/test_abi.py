@@ -174,8 +174,15 @@ def test_selector_64_channel_pair():
     # 65 channels and up: the M = 256 kernel, 128 channels per CTA
     assert cwg.select(4, c, 65, 56, 56).cout_per_cta == 128
     assert cwg.weight_bytes(c, 65, 2) == 1 * 2 * 6 * 16 * 2 * 4096
-    # F(4,3) and the single-CTA ablations keep their layouts
+    # F(4,3) likewise: up to 64 channels, two output rows x 64 channels per CTA
+    # in one pass over all 36 frequencies ([1][2 ranks][6][36 f] fp16 blocks of 128
+    # rows); above, 128 channels of one row per CTA in two passes of 30 frequencies
     assert cwg.select(4, c, k, 56, 56, 4, cwg.BF16).cout_per_cta == 64
+    assert cwg.weight_bytes(c, k, 4, cwg.BF16) == 1 * 2 * 6 * 36 * 1 * 4096
+    assert cwg.weight_bytes(c, k, 4, cwg.BF16 | cwg.TC_X3) == 1 * 2 * 6 * 36 * 2 * 4096
+    assert cwg.select(4, c, 65, 56, 56, 4, cwg.BF16).cout_per_cta == 128
+    assert cwg.weight_bytes(c, 65, 4, cwg.BF16) == 1 * 2 * 2 * 6 * 30 * 1 * 4096
+    # the single-CTA ablations keep their layouts
     assert cwg.select(4, c, k, 56, 56, 2, cwg.TC_NOPAIR).cout_per_cta == 128
 
 
@@ -214,14 +221,16 @@ def test_selector_f43_tensor_core():
     tiles = n * 8 * 8  # 4x4 output tiles
     ch = cwg.select(n, c, k, h, w, 4, cwg.BF16)
     assert ch.path == cwg.PATH_TC and ch.m == 4 and ch.mma_products == 2
-    assert ch.tiles_per_cta == 64 and ch.cout_per_cta == 64
-    assert ch.ctas == 2 * (-(-tiles // 64)) * (-(-k // 64))
-    # weights: [ceil(C_out/64)][2 ranks][C_in/16][36 f] fp16 blocks of 128 rows
-    # (2 output rows x 64 channels) x 16 channels; CWG_TC_X3: bf16 hi and lo blocks
-    assert cwg.weight_bytes(c, k, 4, cwg.BF16) == 4 * 2 * 8 * 36 * 4096
+    assert ch.tiles_per_cta == 64 and ch.cout_per_cta == 128
+    # a CTA pair per (64-tile block, 128-channel block, pass of two output rows)
+    assert ch.ctas == 2 * 2 * (-(-tiles // 64)) * (-(-k // 128))
+    # weights: [ceil(C_out/128)][2 passes][2 ranks][C_in/16][30 f] fp16 blocks of
+    # 128 rows (128 channels of one output row) x 16 channels; a pass stores the
+    # 30 frequencies its At rows do not zero; CWG_TC_X3: bf16 hi and lo blocks
+    assert cwg.weight_bytes(c, k, 4, cwg.BF16) == 2 * 2 * 2 * 8 * 30 * 4096
     x3 = cwg.select(n, c, k, h, w, 4, cwg.BF16 | cwg.TC_X3)
     assert x3.path == cwg.PATH_TC and x3.mma_products == 3
-    assert cwg.weight_bytes(c, k, 4, cwg.BF16 | cwg.TC_X3) == 4 * 2 * 8 * 36 * 2 * 4096
+    assert cwg.weight_bytes(c, k, 4, cwg.BF16 | cwg.TC_X3) == 2 * 2 * 2 * 8 * 30 * 2 * 4096
     # bf16 F(2,3) runs single products; fp32 F(2,3) the hi/lo split
     assert cwg.select(n, c, k, h, w, 0, cwg.BF16).mma_products == 1
     assert cwg.select(n, c, k, h, w, 2).mma_products == 3

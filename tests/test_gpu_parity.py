@@ -321,7 +321,7 @@ F43_TC = [(2, 64, 64, 9, 13), (1, 96, 200, 7, 7), (3, 128, 64, 5, 22), (1, 64, 1
 @pytest.mark.parametrize("products", [0, cwg.TC_X3], ids=["fp16x2", "bf16x3"])
 @pytest.mark.parametrize("case", F43_TC, ids=lambda c: "x".join(map(str, c)))
 def test_tensor_core_f43_bf16(cuda_dev, case, products):
-    """F(4,3) on the pair kernel (6 accumulators, two output rows per CTA) for
+    """F(4,3) on the pair kernel (6 accumulators, one output row per CTA and pass) for
     bf16 layers, in both product modes (fp16 U * (V_hi + V_lo), the default, and
     the bf16 hi/lo split of CWG_TC_X3): ragged tiles, partial channel blocks,
     tile blocks across images."""
@@ -372,11 +372,12 @@ PERSISTENT = [
     (13, 64, 136, 56, 56, 2, 0),                    # fp32 F(2,3), 2 ragged channel blocks
     (13, 64, 64, 56, 56, 2, cwg.BF16),               # bf16 F(2,3): patches outside the V ring
     (13, 96, 64, 56, 56, 2, 0),                      # fp32 F(2,3), 64 channels: M = 128 pair
-    (25, 64, 72, 56, 56, 4, cwg.BF16),               # bf16 F(4,3), 2 ragged channel blocks
+    (25, 64, 72, 56, 56, 4, cwg.BF16),               # bf16 F(4,3): a ragged block, 2 passes
     # below one wave of units: equal runs shorter than an item on more pairs
     (4, 128, 128, 56, 56, 2, 0),                     # 25 blocks -> 66 runs of 48 tiles
     (8, 64, 128, 37, 41, 2, 0),                      # odd image sizes: runs across rows
-    (2, 64, 64, 64, 60, 4, cwg.BF16),                # F(4,3): runs of 32-tile items
+    (2, 64, 64, 64, 60, 4, cwg.BF16),                # F(4,3), 64 channels: runs of 32 tiles
+    (10, 64, 128, 64, 60, 4, cwg.BF16),              # F(4,3), 2 passes: 76 units, runs
 ]
 
 
