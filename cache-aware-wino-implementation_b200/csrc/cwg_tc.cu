@@ -884,25 +884,25 @@ __global__ void wt_transform_tc_pair(const float *__restrict__ src, uint8_t *__r
     for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int il = 0; il < G::kRowsI; ++il) {
-      const long blk0 = (((long)kb * G::kPasses + pass) * 2 + r) * C16 + c / kCc;
-      const uint32_t off = blk_off(il * G::kCoutCta + kr, c % kCc);
+        const long blk0 = (((long)kb * G::kPasses + pass) * 2 + r) * C16 + c / kCc;
+        const uint32_t off = blk_off(il * G::kCoutCta + kr, c % kCc);
 #pragma unroll
-      for (int fp = 0; fp < G::NFP; ++fp) {
-        const int f = G::f0(pass) + fp;
-        const float s = Wino<M>::at((2 * pass + r) * G::kRowsI + il, f / TD) * u[f];
-        uint8_t *b = U + ((blk0 * G::NFP + fp) * parts) * G::kBlkBytes;
-        if constexpr (P::kF16) {
-          *reinterpret_cast<__half *>(b + off) = __float2half_rn(s);
-          umax = fmaxf(umax, fabsf(s));
-        } else {
-          const __nv_bfloat16 hi = __float2bfloat16_rn(s);
-          *reinterpret_cast<__nv_bfloat16 *>(b + off) = hi;
-          if (P::kUParts == 2)
-            *reinterpret_cast<__nv_bfloat16 *>(b + G::kBlkBytes + off) =
-                __float2bfloat16_rn(s - __bfloat162float(hi));
+        for (int fp = 0; fp < G::NFP; ++fp) {
+          const int f = G::f0(pass) + fp;
+          const float s = Wino<M>::at((2 * pass + r) * G::kRowsI + il, f / TD) * u[f];
+          uint8_t *b = U + ((blk0 * G::NFP + fp) * parts) * G::kBlkBytes;
+          if constexpr (P::kF16) {
+            *reinterpret_cast<__half *>(b + off) = __float2half_rn(s);
+            umax = fmaxf(umax, fabsf(s));
+          } else {
+            const __nv_bfloat16 hi = __float2bfloat16_rn(s);
+            *reinterpret_cast<__nv_bfloat16 *>(b + off) = hi;
+            if (P::kUParts == 2)
+              *reinterpret_cast<__nv_bfloat16 *>(b + G::kBlkBytes + off) =
+                  __float2bfloat16_rn(s - __bfloat162float(hi));
+          }
         }
       }
-    }
   if (P::kF16 && !(umax <= kF16Max)) atomicOr(&g_tc_status, kStatusRange);
 }
 
