@@ -434,7 +434,9 @@ def test_small_cin_layers(cuda_dev, case):
 @pytest.mark.parametrize("case", [
     (128, 200, 2, 0), (128, 200, 2, cwg.BF16), (128, 200, 2, cwg.TC_NOPAIR),
     (128, 200, 2, cwg.TC_FULL16), (96, 200, 4, cwg.BF16), (32, 40, 2, 0), (32, 40, 4, cwg.BF16),
-    (80, 64, 2, 0), (80, 64, 2, cwg.BF16)],  # the 64-channel pair kernel's 64-row blocks
+    (80, 64, 2, 0), (80, 64, 2, cwg.BF16),  # the 64-channel pair kernel's 64-row blocks
+    (96, 200, 4, cwg.BF16 | cwg.TC_X3),  # F(4,3) in two passes, bf16 hi and lo
+    (80, 64, 4, cwg.BF16), (80, 64, 4, cwg.BF16 | cwg.TC_X3)],  # F(4,3), 64 channels, one pass
     ids=lambda c: f"c{c[0]}k{c[1]}m{c[2]}f{c[3]:#x}")
 def test_weight_transform_stays_in_its_buffer(cuda_dev, case):
     """Every weight layout is written exactly inside cwg_weight_bytes: guard
