@@ -796,9 +796,11 @@ constexpr unsigned kStatusRange = 2u;
 //           N = 128, 4 accumulators Z[r][b] x 128 columns.
 //   F(4,3): two passes (items) per channel block; in pass p rank r holds the
 //           128 rows of output row i = 2p + r (output channel), 32 tiles of V;
-//           N = 64, 6 accumulators x 64 columns.  (Two rows x 64 channels per
-//           rank and all 36 frequencies, the earlier form: 1346 vs 1272 us on
-//           32 images of 256->256 at 112x112.)
+//           N = 64, 6 accumulators x 64 columns.  Layers of at most 64 output
+//           channels (RP = 2) keep one pass of two rows x 64 channels per rank
+//           over all 36 frequencies, which is also what every F(4,3) layer ran
+//           before the passes (1346 vs 1272 us on 32 images of 256->256 at
+//           112x112).
 //   HM ("half M", F(2,3) layers of at most 64 output channels): M = 128, rank r
 //           holds 64 rows (i = r, output channel); in TMEM the accumulator's
 //           columns [0, N/2) sit in lanes 0-63 and [N/2, N) in lanes 64-127,
