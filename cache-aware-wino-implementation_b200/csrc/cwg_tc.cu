@@ -791,6 +791,22 @@ struct Prod {
 constexpr float kF16Max = 65504.f;
 constexpr unsigned kStatusRange = 2u;
 
+// r = Bt x for F(4x4,3x3) (Bt rows 4 0 -5 0 1 0 / 0 -4 -4 1 1 0 / 0 4 -4 -1 1 0 /
+// 0 -2 -1 2 1 0 / 0 2 -1 -2 1 0 / 0 4 0 -5 0 1), factored over the sums and
+// differences the rows share: 6 additions and 8 multiply-adds.
+template <typename T>
+__device__ __forceinline__ void bt6(const T &x, float (&r)[6]) {
+  const float a = x[1] + x[2], b = x[3] + x[4];
+  const float c = x[1] - x[2], d = x[4] - x[3];
+  const float e = x[4] - x[2], f = x[3] - x[1];
+  r[0] = fmaf(4.f, x[0], fmaf(-5.f, x[2], x[4]));
+  r[1] = fmaf(-4.f, a, b);
+  r[2] = fmaf(4.f, c, d);
+  r[3] = fmaf(2.f, f, e);
+  r[4] = fmaf(-2.f, f, e);
+  r[5] = fmaf(4.f, x[1], fmaf(-5.f, x[3], x[5]));
+}
+
 // Geometry of the pair kernel for F(M x M, 3x3).
 //   F(2,3): rank r holds the 128 rows (i = r, output channel), 64 tiles of V;
 //           N = 128, 4 accumulators Z[r][b] x 128 columns.
@@ -1546,43 +1562,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM, RP>::
             put_v(vb, f, e);
           }
         } else {
-          // Bt d Bt^T: the row pass runs in place, then each output row a is
-          // formed, packed and stored, so two 6x6 windows fit the registers.
+          // Bt d Bt^T with the factored 6-point transform (14 operations instead
+          // of 22 multiply-adds): the row pass runs in place, then each column
+          // b is transformed and its six frequencies packed and stored, so two
+          // 6x6 windows fit the registers.
 #pragma unroll
           for (int q = 0; q < CPT; ++q)
 #pragma unroll
             for (int i = 0; i < TD; ++i) {
               float w[TD];
-#pragma unroll
-              for (int b = 0; b < TD; ++b) {
-                float acc = 0.f;
-#pragma unroll
-                for (int j = 0; j < TD; ++j) {
-                  const float cf = Wino<M>::bt(b, j);
-                  if (cf != 0.f) acc = fmaf(cf, d[q][i][j], acc);
-                }
-                w[b] = acc;
-              }
+              bt6(d[q][i], w);
 #pragma unroll
               for (int b = 0; b < TD; ++b) d[q][i][b] = w[b];
             }
 #pragma unroll
-          for (int a = 0; a < TD; ++a)
+          for (int b = 0; b < TD; ++b) {
+            float col[CPT][TD], r[CPT][TD];
 #pragma unroll
-            for (int b = 0; b < TD; ++b) {
+            for (int q = 0; q < CPT; ++q) {
+#pragma unroll
+              for (int i = 0; i < TD; ++i) col[q][i] = d[q][i][b];
+              bt6(col[q], r[q]);
+            }
+#pragma unroll
+            for (int a = 0; a < TD; ++a) {
               float e[CPT];
 #pragma unroll
-              for (int q = 0; q < CPT; ++q) {
-                float acc = 0.f;
-#pragma unroll
-                for (int i = 0; i < TD; ++i) {
-                  const float cf = Wino<M>::bt(a, i);
-                  if (cf != 0.f) acc = fmaf(cf, d[q][i][b], acc);
-                }
-                e[q] = acc;
-              }
+              for (int q = 0; q < CPT; ++q) e[q] = r[q][a];
               put_v(vb, a * TD + b, e);
             }
+          }
         }
       }
       fence_proxy_async();
