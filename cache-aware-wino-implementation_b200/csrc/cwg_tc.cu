@@ -785,6 +785,34 @@ struct Prod {
 constexpr float kF16Max = 65504.f;
 constexpr unsigned kStatusRange = 2u;
 
+// Division of a non-negative int below 2^31 by a divisor fixed for the launch,
+// as a multiply-high: with l = ceil(log2 d) and m = floor(2^32 (2^l - d) / d) + 1,
+// n / d = (umulhi(m, n) + n) >> l (Granlund and Montgomery, "Division by
+// invariant integers using multiplication", 1994; the sum stays below 2^32 for
+// n < 2^31).  Tile indices and their remainders within an image take it.
+struct FastDiv {
+  uint32_t m, l;
+};
+__host__ __device__ inline FastDiv fast_div(uint32_t d) {
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  return FastDiv{(uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1), l};
+}
+__device__ __forceinline__ int fdiv(int n, FastDiv f) {
+  return (int)((__umulhi(f.m, (uint32_t)n) + (uint32_t)n) >> f.l);
+}
+// n / d: the multiply-high form in the F(2,3) kernels (measured 169.4 vs 171.3 and
+// 173.0 vs 174.6 us on 64 images of 128->128 at 56x56), the plain division in
+// F(4,3), where the multiply-high form measured no faster (32 images of 256->256
+// at 112x112: 1254 vs 1229 us, then 1246 vs 1249 us)
+template <int M>
+__device__ __forceinline__ int tile_div(int n, int d, FastDiv f) {
+  if constexpr (M == 2)
+    return fdiv(n, f);
+  else
+    return n / d;
+}
+
 // r = Bt x for F(4x4,3x3) (Bt rows 4 0 -5 0 1 0 / 0 -4 -4 1 1 0 / 0 4 -4 -1 1 0 /
 // 0 -2 -1 2 1 0 / 0 2 -1 -2 1 0 / 0 4 0 -5 0 1), factored over the sums and
 // differences the rows share: 6 additions and 8 multiply-adds.
@@ -1016,7 +1044,8 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
                                            const float *__restrict__ bias, Tio *__restrict__ y,
                                            int K, int H, int W, int tiles_y, int tiles_x,
                                            int total_tiles, int chunk, int kb_count,
-                                           int relu, int split) {
+                                           int relu, int split, FastDiv fd_img,
+                                           FastDiv fd_tx) {
   using L = PairLayout<M, PM, HM, RP>;
   using G = PairGeo<M, HM, RP>;
   constexpr int TD = G::TD, kN = G::kN, kNU = L::kNU;
@@ -1119,9 +1148,9 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
         long long o = -1;
         if (tt < lim) {
           const int TT = it.t0 + tt;
-          const int nn = TT / per_img;
+          const int nn = tile_div<M>(TT, per_img, fd_img);
           const int rem = TT - nn * per_img;
-          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
+          const int yy = tile_div<M>(rem, tiles_x, fd_tx), xx = rem - yy * tiles_x;
           const int oy = M * yy + irow, ox = M * xx;
           if (oy < H && ox + M <= W)
             o = ((long long)nn * K + kq) * (long long)plane + (long long)oy * W + ox;
@@ -1154,9 +1183,9 @@ __device__ __noinline__ bool pair_epilogue(int e, bool run, int nst, uint8_t *sm
         const int tt = cb + lane / M, j = lane % M;  // lane = pixel
         if (tt < lim) {
           const int TT = it.t0 + tt;
-          const int nn = TT / per_img;
+          const int nn = tile_div<M>(TT, per_img, fd_img);
           const int rem = TT - nn * per_img;
-          const int yy = rem / tiles_x, xx = rem - yy * tiles_x;
+          const int yy = tile_div<M>(rem, tiles_x, fd_tx), xx = rem - yy * tiles_x;
           const int oy = M * yy + irow, ox = M * xx + j;
           if (oy < H && ox < W) {
             Tio *dst = y + ((size_t)nn * K + kq) * plane + (size_t)oy * W + ox;
@@ -1201,7 +1230,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM, RP>::
     wino_fused_tc_pair(const Tio *__restrict__ x, const uint8_t *__restrict__ U,
                        const float *__restrict__ bias, Tio *__restrict__ y, int C, int K, int H,
                        int W, int tiles_y, int tiles_x, int total_tiles, int relu,
-                       int cs_per_split, int split, int chunk, int kb_count) {
+                       int cs_per_split, int split, int chunk, int kb_count,
+                       FastDiv fd_img, FastDiv fd_tx) {
   using L = PairLayout<M, PM, HM, RP>;
   using G = PairGeo<M, HM, RP>;
   constexpr int UP = L::P::kUParts, TD = G::TD, NF = G::NF;
@@ -1440,9 +1470,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM, RP>::
       const bool tile_ok = t < cnt_cta;
       if (tile_ok) {
         const int T = it.t0 + (int)rank * half + t;
-        n = T / per_img;
+        n = tile_div<M>(T, per_img, fd_img);
         const int rem = T - n * per_img;
-        ty = rem / tiles_x;
+        ty = tile_div<M>(rem, tiles_x, fd_tx);
         tx = rem - ty * tiles_x;
       }
       const int y0 = M * ty - 1, x0 = M * tx - 1;
@@ -1534,7 +1564,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM, RP>::
       // overlapped the last MMAs and the epilogue)
       while (ep < n_items && s > (ep + 1) * nst)
         ok = pair_epilogue<M, PM, Tio, HM, RP>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y,
-                                           tiles_x, total_tiles, chunk, kb_count, relu, split) &&
+                                           tiles_x, total_tiles, chunk, kb_count, relu, split, fd_img,
+                                           fd_tx) &&
              ok;
       if (!ok) break;
       const int vs = s % kNV;
@@ -1600,7 +1631,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairGeo<M, HM, RP>::
     }
     while (ep < n_items)
       ok = pair_epilogue<M, PM, Tio, HM, RP>(ep++, ok, nst, smem, bias, y, K, H, W, tiles_y, tiles_x,
-                                         total_tiles, chunk, kb_count, relu, split) &&
+                                         total_tiles, chunk, kb_count, relu, split, fd_img, fd_tx) &&
            ok;
     if (n_items == 0) named_bar_sync(kBarTmem, 32 + kEpiThreads);
     if constexpr (PM == kPmH2) {
@@ -1809,7 +1840,8 @@ static cudaError_t launch_pair(const void *x, const void *U, const float *bias, 
   cfg.numAttrs = (allow_pdl && splits == 1) ? 1 : 0;
   e = cudaLaunchKernelEx(&cfg, fn, (const Tio *)x, (const uint8_t *)U, bias, (Tio *)y, c, k, h, w,
                          tiles_y, tiles_x, (int)total, relu, per, (int)(splits > 1),
-                         (int)plan.chunk, plan.kb_count);
+                         (int)plan.chunk, plan.kb_count,
+                         fast_div((uint32_t)(tiles_y * tiles_x)), fast_div((uint32_t)tiles_x));
   if (e != cudaSuccess || (e = cudaGetLastError()) != cudaSuccess || splits == 1) return e;
   if (relu) e = launch_bias_relu((float *)y, bias, n, k, h, w, relu, sms, s);
   return e;
